@@ -1,0 +1,94 @@
+/* qrb200 -- B200-native batched square QR factorization, C ABI.
+ *
+ * Drop-in replacement for the reference entry point
+ *     custom_kernel(data) -> (H, tau)        reflection_no_reflectors.py:181-196
+ * (johnzfitch/qr-contest).  Output contract = torch.geqrf / LAPACK compact layout:
+ * R in the upper triangle of H (including the diagonal), unit-lower Householder tails
+ * strictly below it, tau_k = 2 / (v_k^T v_k) in [1, 2].  All pointers are DEVICE
+ * pointers of the current CUDA device; everything is enqueued on `stream`
+ * (a cudaStream_t passed as void*, NULL = legacy default stream).
+ *
+ * Nothing in this header depends on PyTorch or on the CUDA headers.
+ */
+#ifndef QRB200_H
+#define QRB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes returned by every entry point */
+#define QRB200_OK 0
+#define QRB200_ERR_INVALID_ARG 1   /* null pointer, negative batch, bad dtype */
+#define QRB200_ERR_UNSUPPORTED_N 2 /* n outside [0, qrb200_max_n()] */
+#define QRB200_ERR_WORKSPACE 3     /* workspace given but smaller than required */
+#define QRB200_ERR_CUDA 4          /* a CUDA runtime call or kernel launch failed */
+
+/* element types of A / H / tau (the factors are always computed in float32) */
+#define QRB200_F32 0
+#define QRB200_BF16 1
+#define QRB200_F16 2
+
+/* per-matrix info bits written to info[b] (0 = clean) */
+#define QRB200_INFO_NONFINITE_INPUT 1 /* NaN/Inf met in the LU stage */
+#define QRB200_INFO_CHOL1_NOT_PD 2    /* 1st CholeskyQR Gram not positive definite after jitter */
+#define QRB200_INFO_CHOL2_NOT_PD 4    /* 2nd pass */
+#define QRB200_INFO_LU_ZERO_PIVOT 8   /* exactly singular column met (informational) */
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int qrb200_version(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* qrb200_status_string(int status);
+
+/* Largest supported order n. */
+int32_t qrb200_max_n(void);
+
+/* Bytes of device workspace qrb200_geqrf_batched needs for (batch, n).
+ * Replaces nothing in the reference (torch allocates internally); callers that manage
+ * memory themselves size the buffer with this. */
+int qrb200_workspace_bytes(int64_t batch, int32_t n, size_t* bytes);
+
+/* Batched QR of `batch` row-major n x n matrices.
+ *   A     [batch][n][n]  input, element type `dtype`, not modified
+ *   H     [batch][n][n]  output, element type `dtype`
+ *   tau   [batch][n]     output, element type `dtype`
+ *   info  [batch]        output, QRB200_INFO_* bits (int32)
+ *   workspace            device buffer of >= qrb200_workspace_bytes() bytes, or NULL to let
+ *                        the library allocate it stream-ordered (cudaMallocAsync) per call
+ * Replaces custom_kernel (reflection_no_reflectors.py:181-196): the frame
+ * (_frame :55-81 -- torch.linalg.lu, two CholeskyQR passes), the closure
+ * R = triu(Q^T A) (:186), the chart (_chart :86-176) and the assembly (:192-196).
+ * Asynchronous with respect to the host; returns QRB200_OK once all work is enqueued. */
+int qrb200_geqrf_batched(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
+                         int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/* Same computation as qrb200_geqrf_batched, with every kernel launch bracketed by CUDA
+ * events on `stream`; blocks until the stream is idle and writes the summed device time
+ * (milliseconds) of each kernel family into family_ms[0 .. qrb200_num_families()-1].
+ * Replaces the reference's CUDA-event stage timing (common/bench.py:12-21,
+ * kan_metric/prof_cluster.py) for the benchmark's roofline figures. */
+int qrb200_geqrf_batched_timed(const void* A, void* H, void* tau, int32_t* info,
+                               int64_t batch, int32_t n, int32_t dtype, void* workspace,
+                               size_t workspace_bytes, void* stream, float* family_ms);
+
+/* Number of kernel families reported by qrb200_geqrf_batched_timed, and their names
+ * ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "trsm", "chart_panel",
+ * "chart_trail", "closure").  No reference counterpart (the stage list of
+ * reflection_no_reflectors.py:55-196 as this library splits it into kernels). */
+int32_t qrb200_num_families(void);
+const char* qrb200_family_name(int32_t family);
+
+/* Total number of CUDA kernels this process has launched through the library.
+ * No reference counterpart; used to report launches inside a timed region. */
+long long qrb200_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QRB200_H */

@@ -1,0 +1,392 @@
+// qrb200 -- C ABI and stage orchestration for the batched square QR (sm_100a).
+//
+// Pipeline per matrix (reflection_no_reflectors.py):
+//   I   frame    : A = P L U (PM_PIVOT panels + TrailW)          -> P*L       (:66)
+//                  CholeskyQR pass 1: G = (PL)^T(PL) (Gram), R1 = chol(G + mu I) (PM_CHOL
+//                  panels + TrailSyrk), Q1 = PL R1^{-1} (trsm_rows)             (:68-79)
+//                  CholeskyQR pass 2 on Q1 -> Q = P Q_L  (row order of A)      (:80-81)
+//   III chart    : elimination of I - QS on a copy of Q (PM_CHART panels + TrailW)
+//                  -> strict lower H, s, tau                               (:86-176,:192)
+//   II  closure  : H_upper = s_i * triu(Q^T A)_ij                         (:186,:195)
+// The batch is processed in chunks so that the float32 working set stays bounded.
+#include "../../include/qrb200.h"
+#include "qrb_common.cuh"
+#include "qrb_gemm_simt.cuh"
+#include "qrb_panel.cuh"
+#include "qrb_trsm.cuh"
+
+#include <atomic>
+#include <mutex>
+#include <utility>
+#include <vector>
+
+namespace qrb {
+
+// Kernel families, in the order of the per-family timings qrb200_geqrf_batched_timed returns.
+enum Family : int {
+  F_LU_PANEL = 0, F_LU_TRAIL, F_GRAM, F_CHOL_PANEL, F_CHOL_TRAIL, F_TRSM, F_CHART_PANEL,
+  F_CHART_TRAIL, F_CLOSURE, F_COUNT
+};
+
+static std::atomic<long long> g_launches{0};
+
+// Optional per-launch CUDA-event bracketing (only for the timed entry point).
+struct Prof {
+  cudaStream_t st;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> rec;
+  cudaEvent_t pending = nullptr;
+  int fam = 0;
+  void begin(int f) {
+    fam = f;
+    cudaEventCreate(&pending);
+    cudaEventRecord(pending, st);
+  }
+  void end() {
+    cudaEvent_t e1;
+    cudaEventCreate(&e1);
+    cudaEventRecord(e1, st);
+    rec.push_back({fam, {pending, e1}});
+  }
+  cudaError_t collect(float* ms) {
+    cudaError_t e = cudaStreamSynchronize(st);
+    for (int i = 0; i < F_COUNT; ++i) ms[i] = 0.f;
+    for (auto& r : rec) {
+      float t = 0.f;
+      if (e == cudaSuccess) e = cudaEventElapsedTime(&t, r.second.first, r.second.second);
+      ms[r.first] += t;
+      cudaEventDestroy(r.second.first);
+      cudaEventDestroy(r.second.second);
+    }
+    rec.clear();
+    return e;
+  }
+};
+
+#define QRB_LAUNCH(prof, fam, ...)        \
+  do {                                   \
+    if (prof) (prof)->begin(fam);        \
+    __VA_ARGS__;                         \
+    if (prof) (prof)->end();             \
+    g_launches.fetch_add(1, std::memory_order_relaxed); \
+  } while (0)
+
+constexpr int kMaxN = 4096;
+constexpr size_t kChunkBudget = size_t(8) << 30;  // float32 working set per chunk
+constexpr int64_t kMaxChunk = 65535;              // grid.y / grid.z limit
+constexpr size_t kPanelSmemCap = 200 * 1024;
+
+static int pick_nb(int n) {
+  for (int w = 32; w >= 8; w >>= 1)
+    if (panel_smem_bytes(n, w) <= kPanelSmemCap) return w;
+  return 0;
+}
+
+static int pick_bmr(int n) {
+  if (trsm_smem_bytes(32, n) <= 72 * 1024) return 32;
+  if (trsm_smem_bytes(16, n) <= 72 * 1024) return 16;
+  if (trsm_smem_bytes(8, n) <= 220 * 1024) return 8;
+  return 0;
+}
+
+static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+
+struct Ws {
+  float *T0, *T1, *L, *R, *Q1, *W, *s, *mu;
+  int *orig, *srcmap;
+};
+
+static size_t per_chunk_bytes(int64_t cb, int n, int nbmax) {
+  const size_t nn = (size_t)n * n;
+  size_t t = 0;
+  t += 5 * align256(cb * nn * sizeof(float));
+  t += align256(cb * (size_t)n * nbmax * sizeof(float));
+  t += align256(cb * (size_t)n * sizeof(float));  // s
+  t += align256(cb * sizeof(float));              // mu
+  t += 2 * align256(cb * (size_t)n * sizeof(int));
+  return t;
+}
+
+static int64_t chunk_of(int64_t batch, int n) {
+  const size_t per = per_chunk_bytes(1, n, 32);
+  int64_t c = (int64_t)(kChunkBudget / per);
+  if (c < 1) c = 1;
+  if (c > kMaxChunk) c = kMaxChunk;
+  return batch < c ? batch : c;
+}
+
+static Ws carve(void* base, int64_t cb, int n, int nbmax) {
+  const size_t nn = (size_t)n * n;
+  char* p = static_cast<char*>(base);
+  Ws w;
+  auto take = [&](size_t bytes) { char* q = p; p += align256(bytes); return q; };
+  w.T0 = (float*)take(cb * nn * sizeof(float));
+  w.T1 = (float*)take(cb * nn * sizeof(float));
+  w.L = (float*)take(cb * nn * sizeof(float));
+  w.R = (float*)take(cb * nn * sizeof(float));
+  w.Q1 = (float*)take(cb * nn * sizeof(float));
+  w.W = (float*)take(cb * (size_t)n * nbmax * sizeof(float));
+  w.s = (float*)take(cb * (size_t)n * sizeof(float));
+  w.mu = (float*)take(cb * sizeof(float));
+  w.orig = (int*)take(cb * (size_t)n * sizeof(int));
+  w.srcmap = (int*)take(cb * (size_t)n * sizeof(int));
+  return w;
+}
+
+static inline dim3 tiles_grid(int M, int N, int64_t cb) {
+  return dim3((N + GT - 1) / GT, (M + GT - 1) / GT, (unsigned)cb);
+}
+
+// Raise the dynamic shared-memory limit of every big-smem kernel once per device.
+template <typename TIn>
+static cudaError_t set_smem_attrs() {
+  const int big = 227 * 1024;
+  cudaError_t e;
+  e = cudaFuncSetAttribute(panel_kernel<PM_PIVOT, TIn, float>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(panel_kernel<PM_CHART, float, TIn>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  return e;
+}
+
+static cudaError_t set_common_attrs() {
+  const int big = 227 * 1024;
+  cudaError_t e;
+  e = cudaFuncSetAttribute(panel_kernel<PM_PIVOT, float, float>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(panel_kernel<PM_CHOL, float, float>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(trsm_rows_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(trsm_rows_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(trsm_rows_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
+  if (e != cudaSuccess) return e;
+  e = set_smem_attrs<float>();
+  if (e != cudaSuccess) return e;
+  e = set_smem_attrs<__nv_bfloat16>();
+  if (e != cudaSuccess) return e;
+  return set_smem_attrs<__half>();
+}
+
+static cudaError_t ensure_attrs() {
+  static std::mutex mu;
+  static bool done[128] = {false};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(mu);
+  if (done[dev]) return cudaSuccess;
+  e = set_common_attrs();
+  if (e == cudaSuccess) done[dev] = true;
+  return e;
+}
+
+static void launch_trsm(const float* M, const float* R, float* X, int n, int64_t cb,
+                        cudaStream_t st, Prof* prof) {
+  const int bmr = pick_bmr(n);
+  const dim3 grid((n + bmr - 1) / bmr, (unsigned)cb);
+  const size_t smem = trsm_smem_bytes(bmr, n);
+  QRB_LAUNCH(prof, F_TRSM,
+             if (bmr == 32) trsm_rows_kernel<32><<<grid, 256, smem, st>>>(M, R, X, n);
+             else if (bmr == 16) trsm_rows_kernel<16><<<grid, 256, smem, st>>>(M, R, X, n);
+             else trsm_rows_kernel<8><<<grid, 256, smem, st>>>(M, R, X, n));
+}
+
+// One CholeskyQR pass: Q = X R^{-1} with R = chol(X^T X + mu I).  G lives in ws.T0.
+static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, const Ws& ws,
+                        int* info, int info_bit, cudaStream_t st, Prof* prof) {
+  QRB_LAUNCH(prof, F_GRAM,
+             simt_gemm_kernel<Gram><<<tiles_grid(n, n, cb), 256, 0, st>>>(GramArgs{n, X, ws.T0}));
+  for (int k0 = 0; k0 < n; k0 += nb) {
+    const int w = (n - k0 < nb) ? n - k0 : nb;
+    PanelArgs pa{};
+    pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
+    pa.src = ws.T0; pa.R = ws.R; pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
+    QRB_LAUNCH(prof, F_CHOL_PANEL,
+               panel_kernel<PM_CHOL, float, float>
+               <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
+    const int k1 = k0 + w;
+    if (k1 < n)
+      QRB_LAUNCH(prof, F_CHOL_TRAIL,
+                 simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                     TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
+  }
+  launch_trsm(X, ws.R, Q, n, cb, st, prof);
+}
+
+template <typename T>
+static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
+                             const Ws& ws, cudaStream_t st, Prof* prof) {
+  const int nb = pick_nb(n);
+  cudaError_t e = cudaMemsetAsync(info, 0, cb * sizeof(int), st);
+  if (e != cudaSuccess) return e;
+
+  // ---- I-a: partial-pivot LU; P*L lands in ws.L ----
+  {
+    const void* cur = A;
+    bool cur_in = true;
+    float* Tb[2] = {ws.T0, ws.T1};
+    int ti = 0;
+    for (int k0 = 0; k0 < n; k0 += nb) {
+      const int w = (n - k0 < nb) ? n - k0 : nb;
+      PanelArgs pa{};
+      pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
+      pa.src = cur; pa.orig = ws.orig; pa.srcmap = ws.srcmap; pa.W = ws.W; pa.L = ws.L;
+      pa.info = info;
+      const size_t smem = panel_smem_bytes(n - k0, w);
+      QRB_LAUNCH(prof, F_LU_PANEL,
+                 if (cur_in) panel_kernel<PM_PIVOT, T, float><<<(unsigned)cb, 256, smem, st>>>(pa);
+                 else panel_kernel<PM_PIVOT, float, float><<<(unsigned)cb, 256, smem, st>>>(pa));
+      const int k1 = k0 + w;
+      if (k1 < n) {
+        TrailWArgs ta{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap};
+        const dim3 g = tiles_grid(n - k1, n - k1, cb);
+        QRB_LAUNCH(prof, F_LU_TRAIL,
+                   if (cur_in) simt_gemm_kernel<TrailW<T>><<<g, 256, 0, st>>>(ta);
+                   else simt_gemm_kernel<TrailW<float>><<<g, 256, 0, st>>>(ta));
+        cur = Tb[ti];
+        ti ^= 1;
+        cur_in = false;
+      }
+    }
+  }
+  // ---- I-b..d: CholeskyQR2 on P*L; the frame Q = P Q_L lands in ws.L ----
+  cholqr_pass(ws.L, ws.Q1, n, cb, nb, ws, info, INFO_CHOL1_NOT_PD, st, prof);
+  cholqr_pass(ws.Q1, ws.L, n, cb, nb, ws, info, INFO_CHOL2_NOT_PD, st, prof);
+
+  // ---- III: chart on a copy of Q (working copy in ws.T0) ----
+  for (int k0 = 0; k0 < n; k0 += nb) {
+    const int w = (n - k0 < nb) ? n - k0 : nb;
+    const float* cur = (k0 == 0) ? ws.L : ws.T0;
+    PanelArgs pa{};
+    pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
+    pa.src = cur; pa.W = ws.W; pa.H = H; pa.tau = tau; pa.s = ws.s; pa.info = info;
+    QRB_LAUNCH(prof, F_CHART_PANEL,
+               panel_kernel<PM_CHART, float, T>
+               <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
+    const int k1 = k0 + w;
+    if (k1 < n)
+      QRB_LAUNCH(prof, F_CHART_TRAIL,
+                 simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                     TrailWArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr}));
+  }
+  // ---- II: closure, H_upper = s * triu(Q^T A) ----
+  QRB_LAUNCH(prof, F_CLOSURE,
+             simt_gemm_kernel<Closure<T>><<<tiles_grid(n, n, cb), 256, 0, st>>>(
+                 ClosureArgs{n, ws.L, A, ws.s, H}));
+  return cudaGetLastError();
+}
+
+template <typename T>
+static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
+                   void* workspace, cudaStream_t st, Prof* prof) {
+  const int64_t cb = chunk_of(batch, n);
+  const int nb = pick_nb(n);
+  const size_t need = per_chunk_bytes(cb, n, nb);
+  void* ws = workspace;
+  bool owned = false;
+  if (!ws) {
+    if (cudaMallocAsync(&ws, need, st) != cudaSuccess) return QRB200_ERR_CUDA;
+    owned = true;
+  }
+  int rc = QRB200_OK;
+  const size_t nn = (size_t)n * n;
+  for (int64_t b0 = 0; b0 < batch; b0 += cb) {
+    const int64_t cnt = (batch - b0 < cb) ? batch - b0 : cb;
+    const Ws w = carve(ws, cnt, n, nb);
+    cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
+                                 static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof);
+    if (e != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
+  }
+  if (owned && cudaFreeAsync(ws, st) != cudaSuccess) rc = QRB200_ERR_CUDA;
+  return rc;
+}
+
+}  // namespace qrb
+
+extern "C" {
+
+int qrb200_version(void) { return 100; }
+
+const char* qrb200_status_string(int status) {
+  switch (status) {
+    case QRB200_OK: return "ok";
+    case QRB200_ERR_INVALID_ARG: return "invalid argument";
+    case QRB200_ERR_UNSUPPORTED_N: return "unsupported matrix order n";
+    case QRB200_ERR_WORKSPACE: return "workspace too small";
+    case QRB200_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int32_t qrb200_max_n(void) { return qrb::kMaxN; }
+
+int qrb200_workspace_bytes(int64_t batch, int32_t n, size_t* bytes) {
+  if (!bytes || batch < 0) return QRB200_ERR_INVALID_ARG;
+  if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
+  if (batch == 0 || n == 0) { *bytes = 0; return QRB200_OK; }
+  const int64_t cb = qrb::chunk_of(batch, n);
+  *bytes = qrb::per_chunk_bytes(cb, n, qrb::pick_nb(n));
+  return QRB200_OK;
+}
+
+static int geqrf_impl(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
+                      int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                      void* stream, qrb::Prof* prof) {
+  if (batch < 0) return QRB200_ERR_INVALID_ARG;
+  if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
+  if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
+    return QRB200_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB200_OK;
+  if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
+  if (workspace) {
+    size_t need = 0;
+    qrb200_workspace_bytes(batch, n, &need);
+    if (workspace_bytes < need) return QRB200_ERR_WORKSPACE;
+  }
+  if (qrb::ensure_attrs() != cudaSuccess) return QRB200_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case QRB200_F32: return qrb::run_all<float>(A, H, tau, info, batch, n, workspace, st, prof);
+    case QRB200_BF16:
+      return qrb::run_all<__nv_bfloat16>(A, H, tau, info, batch, n, workspace, st, prof);
+    default: return qrb::run_all<__half>(A, H, tau, info, batch, n, workspace, st, prof);
+  }
+}
+
+int qrb200_geqrf_batched(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
+                         int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  return geqrf_impl(A, H, tau, info, batch, n, dtype, workspace, workspace_bytes, stream,
+                    nullptr);
+}
+
+int qrb200_geqrf_batched_timed(const void* A, void* H, void* tau, int32_t* info,
+                               int64_t batch, int32_t n, int32_t dtype, void* workspace,
+                               size_t workspace_bytes, void* stream, float* family_ms) {
+  if (!family_ms) return QRB200_ERR_INVALID_ARG;
+  qrb::Prof prof;
+  prof.st = static_cast<cudaStream_t>(stream);
+  const int rc = geqrf_impl(A, H, tau, info, batch, n, dtype, workspace, workspace_bytes,
+                            stream, &prof);
+  const cudaError_t e = prof.collect(family_ms);
+  if (rc != QRB200_OK) return rc;
+  return e == cudaSuccess ? QRB200_OK : QRB200_ERR_CUDA;
+}
+
+int32_t qrb200_num_families(void) { return qrb::F_COUNT; }
+
+const char* qrb200_family_name(int32_t family) {
+  static const char* names[qrb::F_COUNT] = {"lu_panel",    "lu_trail",    "gram",
+                                            "chol_panel",  "chol_trail",  "trsm",
+                                            "chart_panel", "chart_trail", "closure"};
+  return (family >= 0 && family < qrb::F_COUNT) ? names[family] : "unknown";
+}
+
+long long qrb200_launch_count(void) { return qrb::g_launches.load(); }
+
+}  // extern "C"

@@ -1,0 +1,255 @@
+// qrb200 -- panel elimination kernel (one CTA per matrix, panel resident in shared memory).
+//
+// One kernel template serves the three eliminations of the pipeline
+// (reflection_no_reflectors.py):
+//   PM_PIVOT : partial-pivot LU of A (torch.linalg.lu, :66).  Pivot = first row holding the
+//              maximum |a| of the live column (getrf / i?amax semantics).  Rows never move in
+//              HBM: the trailing block is kept "compact" (live rows at [k0,n) in current order)
+//              and the unit-lower factor is written in ORIGINAL row order, i.e. the kernel
+//              emits P*L directly -- the frame Q = P*Q_L (:81) then needs no permutation.
+//   PM_CHOL  : unpivoted LU of the jittered Gram G + mu*I (:74-76), emitting the upper
+//              Cholesky factor R = D^{1/2} L^T row block by row block.  Only the lower
+//              triangle of G is read (the diagonal block is mirrored in shared memory).
+//   PM_CHART : the chart (:144-162): sign rule s_k = +1 iff |1-d| >= |1+d|, pivot 1 + |d|,
+//              multipliers Y[i,k] = -s_k M[i,k] / piv, written straight into H's strict
+//              lower triangle; tau_k = 2 / (1 + sum_{i>k} Y[i,k]^2) (:192).
+// For PM_PIVOT and PM_CHART the kernel also emits W = L21 * L11^{-1} so that the trailing
+// update is the single rank-w product  C22' = C22 - W * C12  (C12 = the panel rows' raw
+// trailing columns), which equals the reference's "forward the panel rows, then
+// M22 -= L21 U12" (:165-174) up to reassociation.
+#pragma once
+#include "qrb_common.cuh"
+#include <float.h>
+#include <limits.h>
+
+namespace qrb {
+
+enum PanelMode : int { PM_PIVOT = 0, PM_CHOL = 1, PM_CHART = 2 };
+
+struct PanelArgs {
+  int n, k0, w, ldw;
+  const void* src;   // current trailing buffer: rows/cols [k0, n) valid (input dtype at k0 == 0)
+  int* orig;         // PIVOT: [b][n] original row id of each current row
+  int* srcmap;       // PIVOT: [b][n] out: new row -> old absolute row in src
+  float* W;          // PIVOT/CHART: [b][n][ldw] out, rows [k0+w, n)
+  float* L;          // PIVOT: [b][n][n] out, P*L (original row order)
+  float* R;          // CHOL: [b][n][n] out, upper rows [k0, k0+w)
+  float* mu;         // CHOL: [b] jitter, computed when k0 == 0
+  void* H;           // CHART: [b][n][n] out (output dtype), strict lower part
+  void* tau;         // CHART: [b][n] out (output dtype)
+  float* s;          // CHART: [b][n] out, signs
+  int* info;         // [b]
+  int info_bit;      // CHOL: bit to raise on a non-positive pivot
+};
+
+// Shared-memory bytes the panel kernel needs for an m-row, w-column panel.
+__host__ __device__ inline size_t panel_smem_bytes(int m, int w) {
+  return (size_t)m * (w + 1) * sizeof(float) + 3 * (size_t)m * sizeof(int) +
+         (size_t)(w + 16) * sizeof(float) + 16 * sizeof(int);
+}
+
+template <int MODE, typename TIn, typename TOut>
+__global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
+  extern __shared__ __align__(16) float sm[];
+  const int n = a.n, k0 = a.k0, w = a.w, m = n - k0, ldp = w + 1;
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  float* P = sm;                                     // [m][ldp]
+  int* lid = reinterpret_cast<int*>(P + (size_t)m * ldp);  // local row permutation
+  int* oid = lid + m;                                // original ids (old order)
+  int* nid = oid + m;                                // original ids (new order)
+  float* dpiv = reinterpret_cast<float*>(nid + m);   // [w] pivots (CHOL) / signs (CHART)
+  float* red_v = dpiv + w;                           // [8]
+  float* red_x = red_v + 8;                          // [8]
+  int* red_i = reinterpret_cast<int*>(red_x + 8);    // [8]
+  int* s_pivrow = red_i + 8;
+  __shared__ int s_flags;
+  __shared__ float s_mu;
+
+  const TIn* src = reinterpret_cast<const TIn*>(a.src) + mat_off(b, n);
+  if (tid == 0) s_flags = 0;
+
+  // ---- jitter (CHOL): mu = 1e-7 * mean(diag G)  (reflection_no_reflectors.py:74) ----
+  if (MODE == PM_CHOL) {
+    if (k0 == 0) {
+      float acc = 0.f;
+      for (int i = tid; i < n; i += 256) acc += to_f32(src[(int64_t)i * n + i]);
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+      if (lane == 0) red_x[warp] = acc;
+      __syncthreads();
+      if (tid == 0) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t += red_x[i];
+        s_mu = 1e-7f * (t / (float)n);
+        a.mu[b] = s_mu;
+      }
+    } else if (tid == 0) {
+      s_mu = a.mu[b];
+    }
+  }
+
+  // ---- load the panel: rows [k0, n), columns [k0, k0 + w) ----
+  for (int idx = tid; idx < m * w; idx += 256) {
+    const int r = idx / w, c = idx - r * w;
+    P[r * ldp + c] = to_f32(src[(int64_t)(k0 + r) * n + k0 + c]);
+  }
+  for (int r = tid; r < m; r += 256) lid[r] = r;
+  __syncthreads();
+  if (MODE == PM_CHOL) {
+    // lower triangle only: mirror the diagonal block, add the jitter on the diagonal
+    for (int idx = tid; idx < w * w; idx += 256) {
+      const int r = idx / w, c = idx - r * w;
+      if (r < c) P[r * ldp + c] = P[c * ldp + r];
+    }
+    __syncthreads();
+    if (tid < w) P[tid * ldp + tid] += s_mu;
+    __syncthreads();
+  }
+
+  // ---- column-by-column elimination inside the panel ----
+  for (int c = 0; c < w; ++c) {
+    if (MODE == PM_PIVOT) {
+      float bv = -1.f;
+      int bi = INT_MAX;
+      bool bad = false;
+      for (int r = c + tid; r < m; r += 256) {
+        const float x = P[r * ldp + c];
+        const float v = fabsf(x);
+        bad |= !isfinite(x);
+        if (v > bv) { bv = v; bi = r; }
+      }
+      if (bad) atomicOr(&s_flags, INFO_NONFINITE_INPUT);
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_down_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_down_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) { red_v[warp] = bv; red_i[warp] = bi; }
+      __syncthreads();
+      if (tid == 0) {
+        float v = red_v[0];
+        int i0 = red_i[0];
+        for (int q = 1; q < 8; ++q)
+          if (red_v[q] > v || (red_v[q] == v && red_i[q] < i0)) { v = red_v[q]; i0 = red_i[q]; }
+        *s_pivrow = (i0 == INT_MAX) ? c : i0;
+      }
+      __syncthreads();
+      const int p = *s_pivrow;
+      if (p != c) {
+        for (int j = tid; j < w; j += 256) {
+          const float t = P[c * ldp + j];
+          P[c * ldp + j] = P[p * ldp + j];
+          P[p * ldp + j] = t;
+        }
+        if (tid == 0) { const int t = lid[c]; lid[c] = lid[p]; lid[p] = t; }
+      }
+      __syncthreads();
+    }
+
+    const float pv = P[c * ldp + c];
+    float scale = 1.f, piv = pv, sgn = 1.f;
+    if (MODE == PM_PIVOT) {
+      // getrf scales the column by the reciprocal pivot; an all-zero column is left as is
+      scale = (pv != 0.f) ? 1.f / pv : 1.f;
+      if (pv == 0.f && tid == 0) atomicOr(&s_flags, INFO_LU_ZERO_PIVOT);
+    } else if (MODE == PM_CHOL) {
+      if (!(pv > 0.f)) {
+        if (tid == 0) atomicOr(&s_flags, a.info_bit);
+        piv = 1.f;  // keep the arithmetic finite; the host reports the failure
+      }
+      if (tid == 0) dpiv[c] = piv;
+    } else {  // PM_CHART
+      const float pp = 1.f - pv, pm = 1.f + pv;
+      sgn = (fabsf(pp) >= fabsf(pm)) ? 1.f : -1.f;
+      piv = (sgn > 0.f) ? pp : pm;
+      if (tid == 0) dpiv[c] = sgn;
+    }
+
+    for (int r = c + 1 + tid; r < m; r += 256) {
+      float* row = P + r * ldp;
+      float l;
+      if (MODE == PM_PIVOT) l = row[c] * scale;
+      else if (MODE == PM_CHOL) l = row[c] / piv;
+      else l = (-sgn * row[c]) / piv;
+      row[c] = l;
+      const float* prow = P + c * ldp;
+      for (int j = c + 1; j < w; ++j) row[j] = fmaf(-l, prow[j], row[j]);
+    }
+    __syncthreads();
+  }
+
+  int* info = a.info + b;
+
+  // ---- outputs ----
+  if (MODE == PM_PIVOT) {
+    int* orig = a.orig + b * n;
+    for (int r = tid; r < m; r += 256) oid[r] = (k0 == 0) ? r : orig[k0 + r];
+    __syncthreads();
+    for (int r = tid; r < m; r += 256) {
+      const int o = oid[lid[r]];
+      nid[r] = o;
+      orig[k0 + r] = o;
+      a.srcmap[b * n + k0 + r] = k0 + lid[r];
+    }
+    __syncthreads();
+    // P*L in original row order: row nid[p] gets columns [k0, k0+w) of L
+    float* L = a.L + mat_off(b, n);
+    for (int p = warp; p < m; p += 8) {
+      float* Lrow = L + (int64_t)nid[p] * n;
+      for (int c = lane; c < w; c += 32)
+        Lrow[k0 + c] = (p > c) ? P[p * ldp + c] : (p == c ? 1.f : 0.f);
+      if (p < w)  // pivot rows are final: zero the rest of their L row
+        for (int j = k0 + w + lane; j < n; j += 32) Lrow[j] = 0.f;
+    }
+  } else if (MODE == PM_CHOL) {
+    float* R = a.R + mat_off(b, n);
+    for (int c = 0; c < w; ++c) {
+      const float sd = sqrtf(dpiv[c]);
+      float* Rrow = R + (int64_t)(k0 + c) * n + k0;
+      for (int p = c + tid; p < m; p += 256)
+        Rrow[p] = (p == c) ? sd : sd * P[p * ldp + c];
+    }
+  } else {  // PM_CHART
+    TOut* H = reinterpret_cast<TOut*>(a.H) + mat_off(b, n);
+    for (int p = warp; p < m; p += 8) {
+      TOut* Hrow = H + (int64_t)(k0 + p) * n + k0;
+      for (int c = lane; c < w && c < p; c += 32) Hrow[c] = from_f32<TOut>(P[p * ldp + c]);
+    }
+    TOut* tau = reinterpret_cast<TOut*>(a.tau) + b * n;
+    for (int c = warp; c < w; c += 8) {
+      float acc = 0.f;
+      for (int p = c + 1 + lane; p < m; p += 32) {
+        const float y = P[p * ldp + c];
+        acc = fmaf(y, y, acc);
+      }
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        tau[k0 + c] = from_f32<TOut>(2.f / (acc + 1.f));
+        a.s[b * n + k0 + c] = dpiv[c];
+      }
+    }
+  }
+
+  // ---- W = L21 * L11^{-1} for the trailing update (PIVOT and CHART) ----
+  if (MODE != PM_CHOL && k0 + w < n) {
+    __syncthreads();
+    for (int p = w + tid; p < m; p += 256) {
+      float* row = P + p * ldp;
+      for (int j = w - 1; j >= 0; --j) {
+        float acc = row[j];
+        for (int i = j + 1; i < w; ++i) acc = fmaf(-row[i], P[i * ldp + j], acc);
+        row[j] = acc;
+      }
+    }
+    __syncthreads();
+    float* W = a.W + (int64_t)b * n * a.ldw;
+    for (int p = w + warp; p < m; p += 8)
+      for (int c = lane; c < w; c += 32) W[(int64_t)(k0 + p) * a.ldw + c] = P[p * ldp + c];
+  }
+
+  __syncthreads();
+  if (tid == 0 && s_flags) atomicOr(info, s_flags);
+}
+
+}  // namespace qrb

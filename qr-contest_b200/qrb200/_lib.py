@@ -1,0 +1,109 @@
+"""ctypes binding of ``libqrb200.so`` (the C ABI declared in ``include/qrb200.h``).
+
+The shared library is built in-tree (``qrb200/build.py``).  Loading it needs no GPU;
+calling the compute entry point does.  There is no fallback: if the library is missing
+the import of :func:`lib` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libqrb200.so"
+
+QRB200_OK = 0
+QRB200_ERR_INVALID_ARG = 1
+QRB200_ERR_UNSUPPORTED_N = 2
+QRB200_ERR_WORKSPACE = 3
+QRB200_ERR_CUDA = 4
+
+QRB200_F32, QRB200_BF16, QRB200_F16 = 0, 1, 2
+
+INFO_NONFINITE_INPUT = 1
+INFO_CHOL1_NOT_PD = 2
+INFO_CHOL2_NOT_PD = 4
+INFO_LU_ZERO_PIVOT = 8
+
+# every symbol include/qrb200.h declares, with its ctypes signature
+SIGNATURES = {
+    "qrb200_version": (ctypes.c_int, []),
+    "qrb200_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "qrb200_max_n": (ctypes.c_int32, []),
+    "qrb200_workspace_bytes": (ctypes.c_int, [ctypes.c_int64, ctypes.c_int32,
+                                              ctypes.POINTER(ctypes.c_size_t)]),
+    "qrb200_geqrf_batched": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+                                            ctypes.c_int32, ctypes.c_void_p, ctypes.c_size_t,
+                                            ctypes.c_void_p]),
+    "qrb200_geqrf_batched_timed": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_void_p, ctypes.c_void_p,
+                                                  ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                                  ctypes.c_void_p, ctypes.c_size_t,
+                                                  ctypes.c_void_p,
+                                                  ctypes.POINTER(ctypes.c_float)]),
+    "qrb200_num_families": (ctypes.c_int32, []),
+    "qrb200_family_name": (ctypes.c_char_p, [ctypes.c_int32]),
+    "qrb200_launch_count": (ctypes.c_longlong, []),
+}
+
+_LIB = None
+
+
+class QRB200Error(RuntimeError):
+    """A non-zero status from the C ABI."""
+
+    def __init__(self, status: int, where: str):
+        self.status = status
+        super().__init__(f"{where}: {status_string(status)} (status {status})")
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is not built; run `python -m qrb200.build` "
+                              "(or __graft_entry__.build())")
+        h = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(h, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = h
+    return _LIB
+
+
+def status_string(status: int) -> str:
+    return lib().qrb200_status_string(int(status)).decode()
+
+
+def workspace_bytes(batch: int, n: int) -> int:
+    out = ctypes.c_size_t(0)
+    rc = lib().qrb200_workspace_bytes(int(batch), int(n), ctypes.byref(out))
+    if rc != QRB200_OK:
+        raise QRB200Error(rc, "qrb200_workspace_bytes")
+    return int(out.value)
+
+
+def geqrf_batched(A_ptr, H_ptr, tau_ptr, info_ptr, batch, n, dtype, ws_ptr, ws_bytes,
+                  stream_ptr) -> int:
+    return lib().qrb200_geqrf_batched(A_ptr, H_ptr, tau_ptr, info_ptr, int(batch), int(n),
+                                      int(dtype), ws_ptr, int(ws_bytes), stream_ptr)
+
+
+def families():
+    L = lib()
+    return [L.qrb200_family_name(i).decode() for i in range(L.qrb200_num_families())]
+
+
+def launch_count() -> int:
+    return int(lib().qrb200_launch_count())
+
+
+def geqrf_batched_timed(A_ptr, H_ptr, tau_ptr, info_ptr, batch, n, dtype, ws_ptr, ws_bytes,
+                        stream_ptr):
+    """Returns (status, {family: ms}); synchronises the stream."""
+    nf = lib().qrb200_num_families()
+    buf = (ctypes.c_float * nf)()
+    rc = lib().qrb200_geqrf_batched_timed(A_ptr, H_ptr, tau_ptr, info_ptr, int(batch), int(n),
+                                          int(dtype), ws_ptr, int(ws_bytes), stream_ptr, buf)
+    return rc, dict(zip(families(), [float(x) for x in buf]))

@@ -1,0 +1,93 @@
+"""Host-side mirror of the reference entry point over the C ABI.
+
+``custom_kernel(data) -> (H, tau)`` follows reflection_no_reflectors.py:181-196:
+
+* input ``(..., n, n)`` of any dtype; the factors are computed in float32
+  (``A = data.to(torch.float32)``, :183) and returned in the input dtype (:196);
+* ``H`` carries ``s_i * R_ij`` on and above the diagonal and the reflector tails below it,
+  ``tau_k = 2 / (1 + ||Y[:, k]||^2)`` (:192-195) -- the torch.geqrf layout;
+* a Gram matrix that is not positive definite after the jitter raises
+  ``torch.linalg.LinAlgError``, as ``torch.linalg.cholesky`` does at :76 (NaN/Inf input
+  ends there too).
+
+Differences that come from the hardware contract: the tensor must live on a CUDA device
+(there is no CPU path), and float32 / bfloat16 / float16 are read and written natively by
+the kernels; any other dtype is converted to float32 on the device first.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+LinAlgError = torch.linalg.LinAlgError
+
+_NATIVE = {torch.float32: _lib.QRB200_F32, torch.bfloat16: _lib.QRB200_BF16,
+           torch.float16: _lib.QRB200_F16}
+
+
+def _prep(data: torch.Tensor):
+    if not isinstance(data, torch.Tensor):
+        raise TypeError("custom_kernel expects a torch.Tensor")
+    if data.dim() < 2 or data.shape[-1] != data.shape[-2]:
+        raise ValueError(f"expected a (..., n, n) tensor, got shape {tuple(data.shape)}")
+    if data.device.type != "cuda":
+        raise ValueError("qrb200 runs on CUDA devices only (got a tensor on "
+                         f"{data.device}); there is no CPU fallback")
+    A = data if data.dtype in _NATIVE else data.to(torch.float32)
+    return A.contiguous()
+
+
+def workspace_bytes(batch: int, n: int) -> int:
+    """Device workspace one :func:`geqrf` call of this shape needs."""
+    return _lib.workspace_bytes(batch, n)
+
+
+def geqrf(data: torch.Tensor, workspace: torch.Tensor | None = None):
+    """Asynchronous core: returns ``(H, tau, info)`` without synchronising the host.
+
+    ``info`` is an int32 tensor of per-matrix ``QRB200_INFO_*`` bits with the leading shape
+    of ``data``.  ``workspace`` (optional) is a uint8 CUDA tensor of at least
+    :func:`workspace_bytes` bytes; when omitted one is taken from torch's caching allocator.
+    """
+    A = _prep(data)
+    lead, n = A.shape[:-2], A.shape[-1]
+    batch = 1
+    for d in lead:
+        batch *= int(d)
+    H = torch.empty_like(A)
+    tau = torch.empty(*lead, n, dtype=A.dtype, device=A.device)
+    info = torch.zeros(*lead, dtype=torch.int32, device=A.device)
+    if batch > 0 and n > 0:
+        need = _lib.workspace_bytes(batch, n)
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=A.device)
+        elif workspace.numel() * workspace.element_size() < need or workspace.device != A.device:
+            raise ValueError(f"workspace must be >= {need} bytes on {A.device}")
+        with torch.cuda.device(A.device):
+            stream = torch.cuda.current_stream(A.device).cuda_stream
+            rc = _lib.geqrf_batched(A.data_ptr(), H.data_ptr(), tau.data_ptr(), info.data_ptr(),
+                                    batch, n, _NATIVE[A.dtype], workspace.data_ptr(),
+                                    need, stream)
+        if rc != _lib.QRB200_OK:
+            raise _lib.QRB200Error(rc, "qrb200_geqrf_batched")
+    if data.dtype not in _NATIVE:
+        H, tau = H.to(data.dtype), tau.to(data.dtype)
+    return H, tau, info
+
+
+def raise_on_info(info: torch.Tensor) -> None:
+    """Raise ``LinAlgError`` like torch.linalg.cholesky would (one device->host read)."""
+    bad = (info & (_lib.INFO_CHOL1_NOT_PD | _lib.INFO_CHOL2_NOT_PD)) != 0
+    if info.numel() and bool(bad.any()):
+        idx = int(bad.reshape(-1).nonzero()[0])
+        raise LinAlgError(
+            f"qrb200: (Batch element {idx}): the Gram matrix of the CholeskyQR frame is not "
+            "positive-definite (non-finite or degenerate input)")
+
+
+def custom_kernel(data: torch.Tensor):
+    """Drop-in for reflection_no_reflectors.custom_kernel: ``(H, tau)`` in data's dtype."""
+    H, tau, info = geqrf(data)
+    raise_on_info(info)
+    return H, tau

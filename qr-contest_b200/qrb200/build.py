@@ -1,0 +1,58 @@
+"""Build ``libqrb200.so`` in-tree with nvcc for sm_100a (no GPU needed to compile).
+
+    python -m qrb200.build            (from the qr-contest_b200 directory)
+
+The library has no PyTorch dependency: plain ``nvcc -shared`` of ``csrc/qrb_api.cu`` with
+the CUDA runtime linked statically.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent                      # qr-contest_b200/
+CSRC = ROOT / "csrc"
+INCLUDE = ROOT.parent / "include"
+LIB = PKG / "libqrb200.so"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
+         "--expt-relaxed-constexpr", "-Xptxas", "-O3"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def sources():
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+
+
+def up_to_date() -> bool:
+    if not LIB.exists():
+        return False
+    t = LIB.stat().st_mtime
+    return all(p.stat().st_mtime <= t for p in sources())
+
+
+def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
+    if not force and up_to_date():
+        return LIB
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-I", str(INCLUDE), "-o", str(LIB),
+           str(CSRC / "qrb_api.cu")]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return LIB
+
+
+if __name__ == "__main__":
+    build(force="--force" in sys.argv, verbose=True,
+          extra=["-Xptxas", "-v"] if "--ptxas-v" in sys.argv else [])

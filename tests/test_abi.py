@@ -1,0 +1,89 @@
+"""CPU: the C-ABI library loads, exports exactly what include/*.h declares, and validates
+its arguments before touching the GPU (every call below returns before any CUDA call)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from qrb200 import _lib
+
+REPO = Path(__file__).resolve().parents[1]
+
+
+def declared_symbols():
+    syms = set()
+    for h in (REPO / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        for m in re.finditer(r"^\s*[A-Za-z_][\w\s\*]*?\b(qrb200_\w+)\s*\(", text, flags=re.M):
+            syms.add(m.group(1))
+    return syms
+
+
+def test_library_exports_every_declared_symbol():
+    L = _lib.lib()
+    syms = declared_symbols()
+    assert syms, "no declarations parsed"
+    assert syms == set(_lib.SIGNATURES), syms ^ set(_lib.SIGNATURES)
+    for s in syms:
+        assert hasattr(L, s), s
+
+
+def test_version_and_limits():
+    L = _lib.lib()
+    assert L.qrb200_version() >= 100
+    assert L.qrb200_max_n() >= 2048
+    assert _lib.status_string(0) == "ok"
+    assert "workspace" in _lib.status_string(_lib.QRB200_ERR_WORKSPACE)
+
+
+def test_workspace_bytes():
+    assert _lib.workspace_bytes(0, 64) == 0
+    assert _lib.workspace_bytes(10, 0) == 0
+    a = _lib.workspace_bytes(1, 64)
+    b = _lib.workspace_bytes(2, 64)
+    assert 5 * 64 * 64 * 4 <= a < b
+    # n=512, batch 1536 fits one chunk: >= 5 float32 n x n buffers per matrix
+    assert _lib.workspace_bytes(1536, 512) >= 1536 * 5 * 512 * 512 * 4
+    with pytest.raises(_lib.QRB200Error):
+        _lib.workspace_bytes(4, 100000)
+    with pytest.raises(_lib.QRB200Error):
+        _lib.workspace_bytes(-1, 8)
+
+
+def _call(**kw):
+    args = dict(A=1, H=1, tau=1, info=1, batch=1, n=8, dtype=0, ws=None, wsb=0, stream=None)
+    args.update(kw)
+    return _lib.geqrf_batched(args["A"], args["H"], args["tau"], args["info"], args["batch"],
+                              args["n"], args["dtype"], args["ws"], args["wsb"], args["stream"])
+
+
+def test_argument_validation_without_gpu():
+    assert _call(batch=-1) == _lib.QRB200_ERR_INVALID_ARG
+    assert _call(n=-3) == _lib.QRB200_ERR_UNSUPPORTED_N
+    assert _call(n=10 ** 6) == _lib.QRB200_ERR_UNSUPPORTED_N
+    assert _call(dtype=9) == _lib.QRB200_ERR_INVALID_ARG
+    assert _call(A=None) == _lib.QRB200_ERR_INVALID_ARG
+    assert _call(info=None) == _lib.QRB200_ERR_INVALID_ARG
+    assert _call(ws=1, wsb=16) == _lib.QRB200_ERR_WORKSPACE
+    # empty problems are a successful no-op
+    assert _call(batch=0, A=None, H=None, tau=None, info=None) == _lib.QRB200_OK
+    assert _call(n=0) == _lib.QRB200_OK
+
+
+def test_no_torch_in_the_abi():
+    text = "".join(h.read_text() for h in (REPO / "include").glob("*.h"))
+    assert not re.search(r"\b(at::|torch::|c10::|Tensor\b)", text)
+    assert "#include <cuda" not in text
+
+
+def test_library_has_no_torch_dependency():
+    # the dynamic section lists no libtorch / libc10 (CUDA runtime is linked statically)
+    import shutil
+    import subprocess
+    if not shutil.which("readelf"):
+        pytest.skip("readelf not available")
+    out = subprocess.run(["readelf", "-d", str(_lib.LIB_PATH)], capture_output=True,
+                         text=True, check=True).stdout
+    needed = [l for l in out.splitlines() if "NEEDED" in l]
+    assert needed and not any(("torch" in l) or ("c10" in l) for l in needed), needed

@@ -1,0 +1,176 @@
+"""GPU parity: the CUDA library (through the C ABI) against the CPU oracle, the golden
+fixtures made from the reference, and the fp64 gates (common/oracle.py:156-195).
+
+Tolerances (float32 pipeline, factors compared elementwise only where they are determined
+to rounding -- rank-deficient inputs have arbitrary null-space columns, gated only):
+  gates   : ||R - Q^T A||_1/||A||_1 < 20 n eps32, ||Q^T Q - I||_1 < 100 n eps32,
+            tau in [1, 2] +- 1e-6   (the north-star gates)
+  tight   : |H - H_ref| <= 2e-4 (1 + |H_ref|), |tau - tau_ref| <= 2e-4
+  illcond : |tau - tau_ref| <= 2e-2 (frame differences scale with cond(A) * eps32)
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import checker, qr_oracle as O
+from tests.golden import fixtures as F
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def qrb():
+    import qrb200
+    return qrb200
+
+
+def run(A):
+    H, tau = qrb().custom_kernel(A.to(DEV))
+    torch.cuda.synchronize()
+    return H, tau
+
+
+def assert_gates(A, H, tau, msg=""):
+    f, o, ftol, otol, passed = checker.check(A.to(DEV), H.to(DEV), tau.to(DEV))
+    assert bool(passed.all()), f"{msg} factor {f / ftol:.3g}x tol, ortho {o / otol:.3g}x tol"
+    return f / ftol, o / otol
+
+
+def assert_tight(H, tau, Href, tref):
+    H, tau = H.float().cpu().numpy(), tau.float().cpu().numpy()
+    err = np.abs(H - Href) / (1.0 + np.abs(Href))
+    assert err.max() <= 2e-4, f"H rel err {err.max():.3g}"
+    assert np.abs(tau - tref).max() <= 2e-4, f"tau err {np.abs(tau - tref).max():.3g}"
+
+
+@pytest.mark.parametrize("name", F.names())
+def test_golden(name):
+    fx = F.load(name)
+    kind = F.kind(name)
+    A = torch.from_numpy(fx["A"])
+    if kind == "bf16":
+        H, tau = run(A.to(torch.bfloat16))
+        assert H.dtype == torch.bfloat16 and tau.dtype == torch.bfloat16
+        np.testing.assert_allclose(H.float().cpu().numpy(), fx["H"], rtol=2 ** -7, atol=2e-3)
+        np.testing.assert_allclose(tau.float().cpu().numpy(), fx["tau"], rtol=2 ** -7, atol=0)
+        # gate the float32 factors of the same input (the bf16 rounding of H/tau itself
+        # breaks tau = 2/v^T v exactness, for the reference as well)
+        H32, t32 = run(A.to(torch.bfloat16).float())
+        assert_gates(A.to(torch.bfloat16).float(), H32, t32, name)
+        return
+    H, tau = run(A)
+    assert_gates(A, H, tau, name)
+    if kind == "tight":
+        assert_tight(H, tau, fx["H"], fx["tau"])
+    elif kind == "loose":
+        assert np.abs(tau.cpu().numpy() - fx["tau"]).max() <= 2e-2
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 5, 8, 17, 31, 32, 33, 47, 64, 65, 100, 127, 128, 129,
+                               200, 256, 300])
+def test_vs_oracle_random(n):
+    g = torch.Generator().manual_seed(1000 + n)
+    b = 8 if n <= 128 else 3
+    A = torch.randn(b, n, n, generator=g, dtype=torch.float64).float()
+    H, tau = run(A)
+    assert_gates(A, H, tau, f"n={n}")
+    Ho, to = O.custom_kernel_np(A.numpy())
+    assert_tight(H, tau, Ho, to)
+
+
+@pytest.mark.parametrize("n", [48, 96, 160])
+def test_classes_vs_oracle(n):
+    from qrb200 import generators as G
+    A = G.heterogeneous(12, n, seed=21, device="cpu")
+    H, tau = run(A)
+    assert_gates(A, H, tau, f"hetero n={n}")
+    Ho, to = O.custom_kernel_np(A.numpy())
+    # dense block (first 2 matrices) is determined to rounding
+    assert_tight(H[:2], tau[:2], Ho[:2], to[:2])
+
+
+def test_leading_dims_and_noncontiguous():
+    g = torch.Generator().manual_seed(5)
+    A = torch.randn(2, 3, 24, 24, generator=g)
+    H, tau = run(A)
+    assert H.shape == (2, 3, 24, 24) and tau.shape == (2, 3, 24)
+    H2, tau2 = run(A.reshape(6, 24, 24))
+    assert torch.equal(H.reshape(6, 24, 24), H2) and torch.equal(tau.reshape(6, 24), tau2)
+    At = A.transpose(-1, -2)  # non-contiguous view
+    H3, tau3 = run(At)
+    H4, tau4 = run(At.contiguous())
+    assert torch.equal(H3, H4) and torch.equal(tau3, tau4)
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float64])
+def test_dtypes(dtype):
+    g = torch.Generator().manual_seed(6)
+    A = torch.randn(4, 40, 40, generator=g).to(dtype)
+    H, tau = run(A)
+    assert H.dtype == dtype and tau.dtype == dtype
+    H32, t32 = run(A.float())
+    ref_H = H32.to(dtype).float()
+    ref_t = t32.to(dtype).float()
+    if dtype == torch.float64:
+        assert torch.equal(H.float(), H32) and torch.equal(tau.float(), t32)
+    else:
+        assert torch.allclose(H.float(), ref_H, rtol=2 ** -8, atol=1e-3)
+        assert torch.allclose(tau.float(), ref_t, rtol=2 ** -8, atol=0)
+
+
+def test_known_answers():
+    n = 37
+    eye = torch.eye(n).expand(3, n, n).contiguous()
+    H, tau = run(eye)
+    assert torch.allclose(H.cpu(), -eye, atol=1e-6) and bool((tau == 2).all())
+    H, tau = run(-eye)
+    assert torch.allclose(H.cpu(), eye, atol=1e-6) and bool((tau == 2).all())
+    g = torch.Generator().manual_seed(7)
+    U = torch.triu(torch.randn(3, n, n, generator=g))
+    H, tau = run(U)
+    assert bool((tau == 2).all()) and bool((torch.tril(H, -1) == 0).all())
+    f, o = assert_gates(U, H, tau)
+    assert f == 0.0
+
+
+def test_multiplier_bound_and_tau_range():
+    g = torch.Generator().manual_seed(8)
+    A = torch.randn(16, 96, 96, generator=g)
+    H, tau = run(A)
+    assert float(torch.tril(H, -1).abs().max()) <= 1.0 + 1e-5
+    assert bool(((tau >= 1 - 1e-6) & (tau <= 2 + 1e-6)).all())
+
+
+def test_deterministic():
+    g = torch.Generator().manual_seed(9)
+    A = torch.randn(64, 80, 80, generator=g).to(DEV)
+    H1, t1 = qrb().custom_kernel(A)
+    H2, t2 = qrb().custom_kernel(A)
+    assert torch.equal(H1, H2) and torch.equal(t1, t2)
+
+
+def test_empty_batch_and_zero_matrix_rows():
+    H, tau = run(torch.zeros(0, 16, 16))
+    assert H.shape == (0, 16, 16) and tau.shape == (0, 16)
+
+
+def test_nonfinite_raises():
+    A = torch.randn(3, 20, 20)
+    A[1, 4, 7] = float("nan")
+    with pytest.raises(torch.linalg.LinAlgError):
+        run(A)
+    _, _, info = qrb().geqrf(A.to(DEV))
+    info = info.cpu()
+    assert int(info[0]) == 0 and int(info[2]) == 0 and int(info[1]) & 1
+
+
+def test_info_clean_on_valid_input():
+    A = torch.randn(10, 50, 50)
+    _, _, info = qrb().geqrf(A.to(DEV))
+    assert int(info.abs().sum()) == 0
+
+
+def test_cpu_tensor_rejected():
+    with pytest.raises(ValueError):
+        qrb().custom_kernel(torch.randn(2, 4, 4))

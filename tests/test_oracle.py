@@ -1,0 +1,111 @@
+"""CPU: the numpy oracle against the reference's own outputs (golden fixtures) and the
+structural known answers of the algorithm (reflection_no_reflectors.py)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import checker, qr_oracle as O
+from tests.golden import fixtures as F
+
+NAMES = F.names()
+
+
+def test_fixtures_present():
+    assert len(NAMES) >= 25
+
+
+@pytest.mark.parametrize("name", NAMES)
+def test_oracle_matches_reference(name):
+    fx = F.load(name)
+    A = fx["A"]
+    kind = F.kind(name)
+    if kind == "bf16":
+        H, tau = O.custom_kernel(torch.from_numpy(A).to(torch.bfloat16))
+        H, tau = H.float().numpy(), tau.float().numpy()
+        # one bf16 ulp of the value (2^-7 relative) where the reference and oracle agree
+        np.testing.assert_allclose(H, fx["H"], rtol=2 ** -7, atol=1e-3)
+        np.testing.assert_allclose(tau, fx["tau"], rtol=2 ** -7, atol=0)
+        return
+    H, tau = O.custom_kernel_np(A)
+    At, Ht, tt = map(torch.from_numpy, (A, H, tau))
+    f, o, ftol, otol, passed = checker.check(At, Ht, tt)
+    assert bool(passed.all()), (f / ftol, o / otol)
+    # the reference itself passes the same gates on these inputs
+    _, _, _, _, ref_pass = checker.check(At, torch.from_numpy(fx["H"]), torch.from_numpy(fx["tau"]))
+    assert bool(ref_pass.all())
+    if kind == "tight":
+        np.testing.assert_allclose(H, fx["H"], rtol=1e-4, atol=1e-4)
+        np.testing.assert_allclose(tau, fx["tau"], rtol=0, atol=1e-4)
+    elif kind == "loose":
+        np.testing.assert_allclose(tau, fx["tau"], rtol=0, atol=2e-2)
+
+
+def test_lu_pivots_match_torch():
+    rng = np.random.default_rng(0)
+    A = rng.standard_normal((4, 45, 45)).astype(np.float32)
+    LU, perm = O.lu_partial_pivot(A)
+    P, L, U = torch.linalg.lu(torch.from_numpy(A))
+    assert (P.numpy().transpose(0, 2, 1).argmax(-1) == perm).all()
+    np.testing.assert_allclose(O.unit_lower(LU), L.numpy(), atol=1e-4)
+    np.testing.assert_allclose(np.triu(LU), U.numpy(), atol=1e-4)
+
+
+def test_cholesky_and_trsm_match_torch():
+    rng = np.random.default_rng(1)
+    X = rng.standard_normal((3, 70, 70)).astype(np.float32)
+    G = X.transpose(0, 2, 1) @ X + 70 * np.eye(70, dtype=np.float32)
+    R, ok = O.cholesky_upper(G)
+    assert ok.all()
+    Rt = torch.linalg.cholesky(torch.from_numpy(G), upper=True).numpy()
+    np.testing.assert_allclose(R, Rt, rtol=1e-4, atol=1e-4)
+    Xs = O.trsm_right_upper(X, R)
+    Xt = torch.linalg.solve_triangular(torch.from_numpy(Rt), torch.from_numpy(X), upper=True,
+                                       left=False).numpy()
+    np.testing.assert_allclose(Xs, Xt, rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("sign", [1.0, -1.0])
+def test_identity_known_answer(sign):
+    # A = +-I  ->  d = +-1, s = -+1, pivot 2, Y = 0: H = -+I, tau = 2
+    A = sign * np.eye(9, dtype=np.float32)[None].repeat(2, 0)
+    H, tau = O.custom_kernel_np(A)
+    np.testing.assert_allclose(H, -A, atol=1e-6)
+    np.testing.assert_array_equal(tau, 2.0)
+
+
+def test_upper_triangular_known_answer():
+    rng = np.random.default_rng(3)
+    A = np.triu(rng.standard_normal((3, 20, 20))).astype(np.float32)
+    H, tau = O.custom_kernel_np(A)
+    np.testing.assert_array_equal(tau, 2.0)
+    np.testing.assert_array_equal(np.tril(H, -1), 0.0)
+    f, o, ftol, otol, passed = checker.check(*map(torch.from_numpy, (A, H, tau)))
+    assert bool(passed.all())
+
+
+def test_multiplier_bound():
+    # pivot >= 1 caps every multiplier: |Y[i,k]| <= |M[i,k]| <= 1 on an orthonormal frame
+    rng = np.random.default_rng(4)
+    A = rng.standard_normal((4, 30, 30)).astype(np.float32)
+    H, tau = O.custom_kernel_np(A)
+    assert np.abs(np.tril(H, -1)).max() <= 1.0 + 1e-5
+    assert ((tau >= 1 - 1e-6) & (tau <= 2 + 1e-6)).all()
+
+
+def test_empty_batch():
+    H, tau = O.custom_kernel_np(np.zeros((0, 5, 5), np.float32))
+    assert H.shape == (0, 5, 5) and tau.shape == (0, 5)
+
+
+def test_checker_flags_bad_factors():
+    rng = np.random.default_rng(5)
+    A = rng.standard_normal((2, 16, 16)).astype(np.float32)
+    H, tau = O.custom_kernel_np(A)
+    H2 = H.copy()
+    H2[:, 0, 5] += 1.0
+    _, _, _, _, passed = checker.check(*map(torch.from_numpy, (A, H2, tau)))
+    assert not bool(passed.any())
+    tau2 = tau.copy()
+    tau2[:, 3] = 2.5
+    _, _, _, _, passed = checker.check(*map(torch.from_numpy, (A, H, tau2)))
+    assert not bool(passed.any())
