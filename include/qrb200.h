@@ -87,6 +87,11 @@ const char* qrb200_family_name(int32_t family);
  * No reference counterpart; used to report launches inside a timed region. */
 long long qrb200_launch_count(void);
 
+/* Text of the last CUDA runtime error that made an entry point of this thread return
+ * QRB200_ERR_CUDA ("no error" if none).  No reference counterpart (torch raises with the
+ * CUDA message). */
+const char* qrb200_last_cuda_error(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,12 @@ enum Family : int {
 };
 
 static std::atomic<long long> g_launches{0};
+static thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+static inline cudaError_t note(cudaError_t e) {
+  if (e != cudaSuccess) g_last_cuda_error = e;
+  return e;
+}
 
 // Optional per-launch CUDA-event bracketing (only for the timed entry point).
 struct Prof {
@@ -139,7 +145,7 @@ static inline dim3 tiles_grid(int M, int N, int64_t cb) {
 // Raise the dynamic shared-memory limit of every big-smem kernel once per device.
 template <typename TIn>
 static cudaError_t set_smem_attrs() {
-  const int big = 227 * 1024;
+  const int big = 225 * 1024;  // leaves room for the kernels' static shared memory
   cudaError_t e;
   e = cudaFuncSetAttribute(panel_kernel<PM_PIVOT, TIn, float>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, big);
@@ -150,7 +156,7 @@ static cudaError_t set_smem_attrs() {
 }
 
 static cudaError_t set_common_attrs() {
-  const int big = 227 * 1024;
+  const int big = 225 * 1024;  // leaves room for the kernels' static shared memory
   cudaError_t e;
   e = cudaFuncSetAttribute(panel_kernel<PM_PIVOT, float, float>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, big);
@@ -290,7 +296,7 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
   void* ws = workspace;
   bool owned = false;
   if (!ws) {
-    if (cudaMallocAsync(&ws, need, st) != cudaSuccess) return QRB200_ERR_CUDA;
+    if (note(cudaMallocAsync(&ws, need, st)) != cudaSuccess) return QRB200_ERR_CUDA;
     owned = true;
   }
   int rc = QRB200_OK;
@@ -300,9 +306,9 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
     const Ws w = carve(ws, cnt, n, nb);
     cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
                                  static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof);
-    if (e != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
+    if (note(e) != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
   }
-  if (owned && cudaFreeAsync(ws, st) != cudaSuccess) rc = QRB200_ERR_CUDA;
+  if (owned && note(cudaFreeAsync(ws, st)) != cudaSuccess) rc = QRB200_ERR_CUDA;
   return rc;
 }
 
@@ -348,7 +354,7 @@ static int geqrf_impl(const void* A, void* H, void* tau, int32_t* info, int64_t 
     qrb200_workspace_bytes(batch, n, &need);
     if (workspace_bytes < need) return QRB200_ERR_WORKSPACE;
   }
-  if (qrb::ensure_attrs() != cudaSuccess) return QRB200_ERR_CUDA;
+  if (qrb::note(qrb::ensure_attrs()) != cudaSuccess) return QRB200_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case QRB200_F32: return qrb::run_all<float>(A, H, tau, info, batch, n, workspace, st, prof);
@@ -388,5 +394,10 @@ const char* qrb200_family_name(int32_t family) {
 }
 
 long long qrb200_launch_count(void) { return qrb::g_launches.load(); }
+
+const char* qrb200_last_cuda_error(void) {
+  const cudaError_t e = qrb::g_last_cuda_error;
+  return e == cudaSuccess ? "no error" : cudaGetErrorString(e);
+}
 
 }  // extern "C"

@@ -44,6 +44,7 @@ SIGNATURES = {
     "qrb200_num_families": (ctypes.c_int32, []),
     "qrb200_family_name": (ctypes.c_char_p, [ctypes.c_int32]),
     "qrb200_launch_count": (ctypes.c_longlong, []),
+    "qrb200_last_cuda_error": (ctypes.c_char_p, []),
 }
 
 _LIB = None
@@ -54,7 +55,10 @@ class QRB200Error(RuntimeError):
 
     def __init__(self, status: int, where: str):
         self.status = status
-        super().__init__(f"{where}: {status_string(status)} (status {status})")
+        msg = f"{where}: {status_string(status)} (status {status})"
+        if status == QRB200_ERR_CUDA:
+            msg += ": " + lib().qrb200_last_cuda_error().decode()
+        super().__init__(msg)
 
 
 def lib() -> ctypes.CDLL:
