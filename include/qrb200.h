@@ -26,6 +26,8 @@ extern "C" {
 #define QRB200_ERR_UNSUPPORTED_N 2 /* n outside [0, qrb200_max_n()] */
 #define QRB200_ERR_WORKSPACE 3     /* workspace given but smaller than required */
 #define QRB200_ERR_CUDA 4          /* a CUDA runtime call or kernel launch failed */
+#define QRB200_ERR_SCRATCH_LIMIT 5 /* allocation-free entry point: one matrix of this order
+                                      needs more than QRB200_NOALLOC_SCRATCH_BYTES */
 
 /* element types of A / H / tau (the factors are always computed in float32) */
 #define QRB200_F32 0
@@ -91,6 +93,26 @@ long long qrb200_launch_count(void);
  * QRB200_ERR_CUDA ("no error" if none).  No reference counterpart (torch raises with the
  * CUDA message). */
 const char* qrb200_last_cuda_error(void);
+
+/* Size of the built-in device scratch of qrb200_geqrf_batched_noalloc (64 MiB). */
+#define QRB200_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+
+/* Allocation-free variant of qrb200_geqrf_batched.  No counterpart in the reference: it is
+ * for callers that cannot allocate device memory when they factor (host callbacks and
+ * allocator hooks where cudaMalloc would re-enter or deadlock, embedders with fully
+ * pre-partitioned memory).  The working buffers live in a file-scope device array of
+ * QRB200_NOALLOC_SCRATCH_BYTES that every GPU loading this library holds until exit; the
+ * batch is factored in chunks that fit it.  The function calls no cudaMalloc, cudaFree or
+ * allocating library routine.
+ *  - Same arguments, results and info bits as qrb200_geqrf_batched (no workspace).
+ *  - Returns QRB200_ERR_SCRATCH_LIMIT when a single n x n problem does not fit the scratch
+ *    (n above 1820 for the 64 MiB array).
+ *  - The first call on each device (with that device current) looks up the array's device
+ *    address; make it before any stream capture.
+ *  - All calls share the array: calls that overlap on the GPU (other streams or threads)
+ *    race and must be serialized by the caller. */
+int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, int32_t* info,
+                                 int64_t batch, int32_t n, int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -325,6 +325,9 @@ const char* qrb200_status_string(int status) {
     case QRB200_ERR_UNSUPPORTED_N: return "unsupported matrix order n";
     case QRB200_ERR_WORKSPACE: return "workspace too small";
     case QRB200_ERR_CUDA: return "CUDA runtime error";
+    case QRB200_ERR_SCRATCH_LIMIT:
+      return "one matrix of this order needs more than the allocation-free entry point's "
+             "built-in scratch (QRB200_NOALLOC_SCRATCH_BYTES)";
     default: return "unknown status";
   }
 }
@@ -401,3 +404,97 @@ const char* qrb200_last_cuda_error(void) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory at the point where they factor: code running
+// inside a host callback or a custom allocator hook (where cudaMalloc/cudaMallocAsync would
+// re-enter the allocator or deadlock), embedders whose memory is fully pre-partitioned, and
+// plug-in hosts that forbid allocation after start-up.  For them this file keeps the
+// working buffers of the pipeline in one file-scope device array of
+// QRB200_NOALLOC_SCRATCH_BYTES bytes, which every GPU that loads this library holds until
+// the process exits.  The caller still owns A, H, tau and info.
+//
+// Host code must not pass the array's name to a kernel: on the host it is only a
+// stand-in symbol, not a device address.  The first call on each device (with that device
+// current) asks the runtime for the array's device address with cudaGetSymbolAddress and
+// caches it; make that first call before any stream capture.
+//
+// Every call shares the array and it keeps the previous call's contents.  Nothing in it has
+// to start at zero: each stage writes every word it later reads (info, which must start at
+// zero, is the caller's buffer and is cleared on the stream per chunk).  Calls that overlap
+// on the GPU (two streams, or two host threads) race on the array; serialize them.
+// ---------------------------------------------------------------------------------------
+namespace qrb {
+
+constexpr size_t kNoAllocScratchBytes = QRB200_NOALLOC_SCRATCH_BYTES;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[128] = {nullptr};
+
+// Device address of g_noalloc_scratch on the current device (looked up once per device).
+static cudaError_t noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+
+// Largest number of matrices whose working set fits the built-in scratch (0 = none).
+static int64_t noalloc_chunk(int n, int nb) {
+  int64_t c = (int64_t)(kNoAllocScratchBytes / per_chunk_bytes(1, n, nb)) + 1;
+  while (c > 0 && per_chunk_bytes(c, n, nb) > kNoAllocScratchBytes) --c;
+  return c < kMaxChunk ? c : kMaxChunk;
+}
+
+template <typename T>
+static int run_noalloc(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
+                       void* scratch, int64_t cb, cudaStream_t st) {
+  const int nb = pick_nb(n);
+  const size_t nn = (size_t)n * n;
+  for (int64_t b0 = 0; b0 < batch; b0 += cb) {
+    const int64_t cnt = (batch - b0 < cb) ? batch - b0 : cb;
+    const Ws w = carve(scratch, cnt, n, nb);
+    cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
+                                 static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st,
+                                 nullptr);
+    if (note(e) != cudaSuccess) return QRB200_ERR_CUDA;
+  }
+  return QRB200_OK;
+}
+
+}  // namespace qrb
+
+extern "C" int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, int32_t* info,
+                                            int64_t batch, int32_t n, int32_t dtype,
+                                            void* stream) {
+  if (batch < 0) return QRB200_ERR_INVALID_ARG;
+  if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
+  if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
+    return QRB200_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB200_OK;
+  if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
+  const int64_t cb = qrb::noalloc_chunk(n, qrb::pick_nb(n));
+  if (cb < 1) return QRB200_ERR_SCRATCH_LIMIT;
+  if (qrb::note(qrb::ensure_attrs()) != cudaSuccess) return QRB200_ERR_CUDA;
+  void* scratch = nullptr;
+  if (qrb::note(qrb::noalloc_scratch(&scratch)) != cudaSuccess) return QRB200_ERR_CUDA;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case QRB200_F32: return qrb::run_noalloc<float>(A, H, tau, info, batch, n, scratch, cb, st);
+    case QRB200_BF16:
+      return qrb::run_noalloc<__nv_bfloat16>(A, H, tau, info, batch, n, scratch, cb, st);
+    default: return qrb::run_noalloc<__half>(A, H, tau, info, batch, n, scratch, cb, st);
+  }
+}

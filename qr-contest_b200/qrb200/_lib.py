@@ -16,6 +16,8 @@ QRB200_ERR_INVALID_ARG = 1
 QRB200_ERR_UNSUPPORTED_N = 2
 QRB200_ERR_WORKSPACE = 3
 QRB200_ERR_CUDA = 4
+QRB200_ERR_SCRATCH_LIMIT = 5
+NOALLOC_SCRATCH_BYTES = 64 << 20
 
 QRB200_F32, QRB200_BF16, QRB200_F16 = 0, 1, 2
 
@@ -45,6 +47,10 @@ SIGNATURES = {
     "qrb200_family_name": (ctypes.c_char_p, [ctypes.c_int32]),
     "qrb200_launch_count": (ctypes.c_longlong, []),
     "qrb200_last_cuda_error": (ctypes.c_char_p, []),
+    "qrb200_geqrf_batched_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
+                                                    ctypes.c_void_p, ctypes.c_void_p,
+                                                    ctypes.c_int64, ctypes.c_int32,
+                                                    ctypes.c_int32, ctypes.c_void_p]),
 }
 
 _LIB = None
