@@ -75,7 +75,7 @@ def nb_for(n: int) -> int:
 def family_flops(n: int) -> dict:
     """Algorithmic flops each kernel family performs on one matrix."""
     nb = nb_for(n)
-    f = {k: 0.0 for k in ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "trsm",
+    f = {k: 0.0 for k in ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "q_apply",
                           "chart_panel", "chart_trail", "closure")}
     for k0 in range(0, n, nb):
         w = min(nb, n - k0)
@@ -89,9 +89,9 @@ def family_flops(n: int) -> dict:
         t = n - k1
         f["lu_trail"] += 2.0 * t * t * w
         f["chart_trail"] += 2.0 * t * t * w
-        f["chol_trail"] += 2 * (t * t * w)  # two passes, symmetric half
+        f["chol_trail"] += 2 * (t * t * w + 2.0 * t * k1 * w)  # two passes: SYRK half + L_G^-1
     f["gram"] = 2.0 * n ** 3            # two Grams, symmetric half each
-    f["trsm"] = 2.0 * n ** 3            # two solves
+    f["q_apply"] = 2.0 * n ** 3         # two passes of X R^{-1} (R^{-1} upper triangular)
     f["closure"] = 1.0 * n ** 3         # upper triangle of Q^T A
     return f
 
@@ -104,14 +104,15 @@ def family_bytes(n: int) -> dict:
         w = min(nb, n - k0)
         m = n - k0
         t = n - k0 - w
+        k1 = k0 + w
         b["lu_panel"] += 4.0 * (m * w + n * w + t * w)
         b["chart_panel"] += 4.0 * (m * w + m * w + t * w)
         b["chol_panel"] += 2 * 4.0 * (m * w + m * w)
         b["lu_trail"] += 4.0 * (2 * t * t + t * w + w * t)
         b["chart_trail"] += 4.0 * (2 * t * t + t * w + w * t)
-        b["chol_trail"] += 2 * 4.0 * (t * t + 2 * t * w)  # lower half read+write
+        b["chol_trail"] += 2 * 4.0 * (t * t + 2 * t * w + 2 * t * k1)  # G lower half, L_G^-1
     b["gram"] = 2 * 4.0 * (n * n + n * n / 2)
-    b["trsm"] = 2 * 4.0 * (2 * n * n + n * n / 2)
+    b["q_apply"] = 4.0 * (2 * n * n + n * n / 2) + 4.0 * (3 * n * n + n * n / 2)
     b["closure"] = 4.0 * (2 * n * n + n * n / 2)
     return b
 

@@ -39,6 +39,7 @@ extern "C" {
 #define QRB200_INFO_CHOL1_NOT_PD 2    /* 1st CholeskyQR Gram not positive definite after jitter */
 #define QRB200_INFO_CHOL2_NOT_PD 4    /* 2nd pass */
 #define QRB200_INFO_LU_ZERO_PIVOT 8   /* exactly singular column met (informational) */
+#define QRB200_INFO_DEVICE_TIMEOUT 16 /* a bounded in-kernel wait expired (never expected) */
 
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int qrb200_version(void);
@@ -79,7 +80,7 @@ int qrb200_geqrf_batched_timed(const void* A, void* H, void* tau, int32_t* info,
                                size_t workspace_bytes, void* stream, float* family_ms);
 
 /* Number of kernel families reported by qrb200_geqrf_batched_timed, and their names
- * ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "trsm", "chart_panel",
+ * ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "q_apply", "chart_panel",
  * "chart_trail", "closure").  No reference counterpart (the stage list of
  * reflection_no_reflectors.py:55-196 as this library splits it into kernels). */
 int32_t qrb200_num_families(void);
@@ -88,6 +89,13 @@ const char* qrb200_family_name(int32_t family);
 /* Total number of CUDA kernels this process has launched through the library.
  * No reference counterpart; used to report launches inside a timed region. */
 long long qrb200_launch_count(void);
+
+/* Process-wide tuning options (no reference counterpart).
+ *   QRB200_OPT_GEMM_PATH: 0 = automatic (tcgen05 3xTF32 tiles when n % 4 == 0 and n >= 128,
+ *   SIMT float32 tiles otherwise), 1 = SIMT tiles only, 2 = tcgen05 tiles whenever n % 4 == 0.
+ * Returns QRB200_ERR_INVALID_ARG for an unknown key or value. */
+#define QRB200_OPT_GEMM_PATH 1
+int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return
  * QRB200_ERR_CUDA ("no error" if none).  No reference counterpart (torch raises with the

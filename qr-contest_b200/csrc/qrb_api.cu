@@ -2,8 +2,9 @@
 //
 // Pipeline per matrix (reflection_no_reflectors.py):
 //   I   frame    : A = P L U (PM_PIVOT panels + TrailW)          -> P*L       (:66)
-//                  CholeskyQR pass 1: G = (PL)^T(PL) (Gram), R1 = chol(G + mu I) (PM_CHOL
-//                  panels + TrailSyrk), Q1 = PL R1^{-1} (trsm_rows)             (:68-79)
+//                  CholeskyQR pass 1: G = (PL)^T(PL) (Gram), G + mu I = L_G D L_G^T
+//                  (PM_CHOL panels + TrailSyrk + LinvTrail), Q1 = PL R1^{-1} with
+//                  R1^{-1} = L_G^{-T} D^{-1/2} (QApply, one GEMM)               (:68-79)
 //                  CholeskyQR pass 2 on Q1 -> Q = P Q_L  (row order of A)      (:80-81)
 //   III chart    : elimination of I - QS on a copy of Q (PM_CHART panels + TrailW)
 //                  -> strict lower H, s, tau                               (:86-176,:192)
@@ -13,7 +14,7 @@
 #include "qrb_common.cuh"
 #include "qrb_gemm_simt.cuh"
 #include "qrb_panel.cuh"
-#include "qrb_trsm.cuh"
+#include "qrb_tc_ops.cuh"
 
 #include <atomic>
 #include <mutex>
@@ -24,11 +25,12 @@ namespace qrb {
 
 // Kernel families, in the order of the per-family timings qrb200_geqrf_batched_timed returns.
 enum Family : int {
-  F_LU_PANEL = 0, F_LU_TRAIL, F_GRAM, F_CHOL_PANEL, F_CHOL_TRAIL, F_TRSM, F_CHART_PANEL,
+  F_LU_PANEL = 0, F_LU_TRAIL, F_GRAM, F_CHOL_PANEL, F_CHOL_TRAIL, F_QAPPLY, F_CHART_PANEL,
   F_CHART_TRAIL, F_CLOSURE, F_COUNT
 };
 
 static std::atomic<long long> g_launches{0};
+static std::atomic<int> g_gemm_path{0};  // 0 auto, 1 SIMT only, 2 tcgen05 wherever legal
 static thread_local cudaError_t g_last_cuda_error = cudaSuccess;
 
 static inline cudaError_t note(cudaError_t e) {
@@ -87,17 +89,10 @@ static int pick_nb(int n) {
   return 0;
 }
 
-static int pick_bmr(int n) {
-  if (trsm_smem_bytes(32, n) <= 72 * 1024) return 32;
-  if (trsm_smem_bytes(16, n) <= 72 * 1024) return 16;
-  if (trsm_smem_bytes(8, n) <= 220 * 1024) return 8;
-  return 0;
-}
-
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Ws {
-  float *T0, *T1, *L, *R, *Q1, *W, *s, *mu;
+  float *T0, *T1, *L, *R, *Q1, *W, *s, *mu, *D;
   int *orig, *srcmap;
 };
 
@@ -108,6 +103,7 @@ static size_t per_chunk_bytes(int64_t cb, int n, int nbmax) {
   t += align256(cb * (size_t)n * nbmax * sizeof(float));
   t += align256(cb * (size_t)n * sizeof(float));  // s
   t += align256(cb * sizeof(float));              // mu
+  t += align256(cb * (size_t)n * sizeof(float));  // D
   t += 2 * align256(cb * (size_t)n * sizeof(int));
   return t;
 }
@@ -133,6 +129,7 @@ static Ws carve(void* base, int64_t cb, int n, int nbmax) {
   w.W = (float*)take(cb * (size_t)n * nbmax * sizeof(float));
   w.s = (float*)take(cb * (size_t)n * sizeof(float));
   w.mu = (float*)take(cb * sizeof(float));
+  w.D = (float*)take(cb * (size_t)n * sizeof(float));
   w.orig = (int*)take(cb * (size_t)n * sizeof(int));
   w.srcmap = (int*)take(cb * (size_t)n * sizeof(int));
   return w;
@@ -141,6 +138,25 @@ static Ws carve(void* base, int64_t cb, int n, int nbmax) {
 static inline dim3 tiles_grid(int M, int N, int64_t cb) {
   return dim3((N + GT - 1) / GT, (M + GT - 1) / GT, (unsigned)cb);
 }
+
+// tcgen05 tiles need float4-aligned rows; small orders stay on the SIMT tiles.
+static inline bool use_tc(int n) {
+  const int p = g_gemm_path.load(std::memory_order_relaxed);
+  if (p == 1) return false;
+  if (p == 2) return (n & 3) == 0;
+  return (n & 3) == 0 && n >= 128;
+}
+
+template <class Pb>
+static cudaError_t tc_attr() {
+  return cudaFuncSetAttribute(tc::tc_gemm_kernel<Pb, 128>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              tc::SmemLayout<128>::TOTAL);
+}
+static inline dim3 tc_grid(int M, int N, int64_t cb) {
+  return dim3((N + 127) / 128, (M + tc::BM - 1) / tc::BM, (unsigned)cb);
+}
+constexpr size_t kTcSmem = tc::SmemLayout<128>::TOTAL;
 
 // Raise the dynamic shared-memory limit of every big-smem kernel once per device.
 template <typename TIn>
@@ -164,17 +180,21 @@ static cudaError_t set_common_attrs() {
   e = cudaFuncSetAttribute(panel_kernel<PM_CHOL, float, float>,
                            cudaFuncAttributeMaxDynamicSharedMemorySize, big);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(trsm_rows_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(trsm_rows_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(trsm_rows_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, big);
-  if (e != cudaSuccess) return e;
   e = set_smem_attrs<float>();
   if (e != cudaSuccess) return e;
   e = set_smem_attrs<__nv_bfloat16>();
   if (e != cudaSuccess) return e;
-  return set_smem_attrs<__half>();
+  e = set_smem_attrs<__half>();
+  if (e != cudaSuccess) return e;
+  if ((e = tc_attr<tc::GramTC>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::QApplyTC>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::SyrkTC>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::ClosureTC<float>>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::ClosureTC<__nv_bfloat16>>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::ClosureTC<__half>>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::TrailWTC<float>>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::TrailWTC<__nv_bfloat16>>()) != cudaSuccess) return e;
+  return tc_attr<tc::TrailWTC<__half>>();
 }
 
 static cudaError_t ensure_attrs() {
@@ -191,43 +211,60 @@ static cudaError_t ensure_attrs() {
   return e;
 }
 
-static void launch_trsm(const float* M, const float* R, float* X, int n, int64_t cb,
-                        cudaStream_t st, Prof* prof) {
-  const int bmr = pick_bmr(n);
-  const dim3 grid((n + bmr - 1) / bmr, (unsigned)cb);
-  const size_t smem = trsm_smem_bytes(bmr, n);
-  QRB_LAUNCH(prof, F_TRSM,
-             if (bmr == 32) trsm_rows_kernel<32><<<grid, 256, smem, st>>>(M, R, X, n);
-             else if (bmr == 16) trsm_rows_kernel<16><<<grid, 256, smem, st>>>(M, R, X, n);
-             else trsm_rows_kernel<8><<<grid, 256, smem, st>>>(M, R, X, n));
-}
-
-// One CholeskyQR pass: Q = X R^{-1} with R = chol(X^T X + mu I).  G lives in ws.T0.
+// One CholeskyQR pass (reflection_no_reflectors.py:68-77): G = X^T X (+ mu I),
+// G = L_G D L_G^T by panels, then Q = X R^{-1} with R^{-1} = L_G^{-T} D^{-1/2}.
+//   pass 1: Q = X R^{-1};  pass 2: Q = X - X (I - R^{-1}) (only the small correction goes
+//   through the tensor cores; the subtraction is float32).
+// The second pass sets the frame's final orthogonality (|q_k|^2 - 1 shows up one-for-one in
+// tau_k = 2/(1+|y_k|^2) when d_k ~ 0), so its Gram diagonal is recomputed in exact float32
+// column sums.  G lives in ws.T0; R (upper) and L_G^{-1} (strict lower) share ws.R.
 static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, const Ws& ws,
                         int* info, int info_bit, cudaStream_t st, Prof* prof) {
+  const bool tcp = use_tc(n);
+  const bool pass2 = (info_bit == INFO_CHOL2_NOT_PD);
   QRB_LAUNCH(prof, F_GRAM,
-             simt_gemm_kernel<Gram><<<tiles_grid(n, n, cb), 256, 0, st>>>(GramArgs{n, X, ws.T0}));
+             if (tcp) tc::tc_gemm_kernel<tc::GramTC, 128><<<tc_grid(n, n, cb), tc::NTHREADS,
+                                                               kTcSmem, st>>>(
+                 tc::GramTCArgs{n, X, ws.T0, info});
+             else simt_gemm_kernel<Gram><<<tiles_grid(n, n, cb), 256, 0, st>>>(
+                 GramArgs{n, X, ws.T0}));
+  if (tcp && pass2)
+    QRB_LAUNCH(prof, F_GRAM,
+               colnorm2_kernel<<<dim3((n + 255) / 256, (unsigned)cb), 256, 0, st>>>(X, ws.T0, n));
   for (int k0 = 0; k0 < n; k0 += nb) {
     const int w = (n - k0 < nb) ? n - k0 : nb;
     PanelArgs pa{};
     pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
-    pa.src = ws.T0; pa.R = ws.R; pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
+    pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = ws.W; pa.mu = ws.mu; pa.info = info;
+    pa.info_bit = info_bit;
     QRB_LAUNCH(prof, F_CHOL_PANEL,
                panel_kernel<PM_CHOL, float, float>
                <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
     const int k1 = k0 + w;
-    if (k1 < n)
+    if (k1 < n) {
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                 if (tcp) tc::tc_gemm_kernel<tc::SyrkTC, 128>
+                     <<<tc_grid(n - k1, n - k1, cb), tc::NTHREADS, kTcSmem, st>>>(
+                         tc::SyrkTCArgs{n, k0, k1, ws.T0, ws.R, info});
+                 else simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
                      TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
+      QRB_LAUNCH(prof, F_CHOL_TRAIL,
+                 simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k1, k1, cb), 256, 0, st>>>(
+                     LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W}));
+    }
   }
-  launch_trsm(X, ws.R, Q, n, cb, st, prof);
+  const QApplyArgs qa{n, pass2 ? 1 : 0, X, ws.R, ws.D, Q, info};
+  QRB_LAUNCH(prof, F_QAPPLY,
+             if (tcp) tc::tc_gemm_kernel<tc::QApplyTC, 128><<<tc_grid(n, n, cb), tc::NTHREADS,
+                                                                kTcSmem, st>>>(qa);
+             else simt_gemm_kernel<QApply><<<tiles_grid(n, n, cb), 256, 0, st>>>(qa));
 }
 
 template <typename T>
 static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
                              const Ws& ws, cudaStream_t st, Prof* prof) {
   const int nb = pick_nb(n);
+  const bool tcp = use_tc(n);
   cudaError_t e = cudaMemsetAsync(info, 0, cb * sizeof(int), st);
   if (e != cudaSuccess) return e;
 
@@ -251,8 +288,14 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
       if (k1 < n) {
         TrailWArgs ta{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap};
         const dim3 g = tiles_grid(n - k1, n - k1, cb);
+        const tc::TrailWTCArgs tca{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap, info};
+        const dim3 gt = tc_grid(n - k1, n - k1, cb);
         QRB_LAUNCH(prof, F_LU_TRAIL,
-                   if (cur_in) simt_gemm_kernel<TrailW<T>><<<g, 256, 0, st>>>(ta);
+                   if (tcp && cur_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, 128>
+                       <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
+                   else if (tcp) tc::tc_gemm_kernel<tc::TrailWTC<float>, 128>
+                       <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
+                   else if (cur_in) simt_gemm_kernel<TrailW<T>><<<g, 256, 0, st>>>(ta);
                    else simt_gemm_kernel<TrailW<float>><<<g, 256, 0, st>>>(ta));
         cur = Tb[ti];
         ti ^= 1;
@@ -275,6 +318,8 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
                panel_kernel<PM_CHART, float, T>
                <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
     const int k1 = k0 + w;
+    // The chart stays on float32 FMA tiles: tau_k = 2/(1+|y_k|^2) sits at 1 when d_k = 0,
+    // and the 2^-21 products of 3xTF32 would push it below the tau >= 1 - 1e-6 gate.
     if (k1 < n)
       QRB_LAUNCH(prof, F_CHART_TRAIL,
                  simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
@@ -282,7 +327,10 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   }
   // ---- II: closure, H_upper = s * triu(Q^T A) ----
   QRB_LAUNCH(prof, F_CLOSURE,
-             simt_gemm_kernel<Closure<T>><<<tiles_grid(n, n, cb), 256, 0, st>>>(
+             if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, 128>
+                 <<<tc_grid(n, n, cb), tc::NTHREADS, kTcSmem, st>>>(
+                     tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
+             else simt_gemm_kernel<Closure<T>><<<tiles_grid(n, n, cb), 256, 0, st>>>(
                  ClosureArgs{n, ws.L, A, ws.s, H}));
   return cudaGetLastError();
 }
@@ -391,12 +439,21 @@ int32_t qrb200_num_families(void) { return qrb::F_COUNT; }
 
 const char* qrb200_family_name(int32_t family) {
   static const char* names[qrb::F_COUNT] = {"lu_panel",    "lu_trail",    "gram",
-                                            "chol_panel",  "chol_trail",  "trsm",
+                                            "chol_panel",  "chol_trail",  "q_apply",
                                             "chart_panel", "chart_trail", "closure"};
   return (family >= 0 && family < qrb::F_COUNT) ? names[family] : "unknown";
 }
 
 long long qrb200_launch_count(void) { return qrb::g_launches.load(); }
+
+int qrb200_set_option(int32_t key, int64_t value) {
+  if (key == QRB200_OPT_GEMM_PATH) {
+    if (value < 0 || value > 2) return QRB200_ERR_INVALID_ARG;
+    qrb::g_gemm_path.store((int)value);
+    return QRB200_OK;
+  }
+  return QRB200_ERR_INVALID_ARG;
+}
 
 const char* qrb200_last_cuda_error(void) {
   const cudaError_t e = qrb::g_last_cuda_error;

@@ -21,6 +21,7 @@ enum InfoBits : int {
   INFO_CHOL1_NOT_PD = 2,      // first CholeskyQR pass: Gram pivot <= 0 after jitter
   INFO_CHOL2_NOT_PD = 4,      // second pass
   INFO_LU_ZERO_PIVOT = 8,     // an exactly singular column (informational, like getrf info>0)
+  INFO_DEVICE_TIMEOUT = 16,   // a bounded in-kernel wait gave up (never expected)
 };
 
 __device__ __forceinline__ float to_f32(float x) { return x; }

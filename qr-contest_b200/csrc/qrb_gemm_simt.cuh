@@ -185,3 +185,94 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(typename Pb::Args a) {
 }
 
 }  // namespace qrb
+
+namespace qrb {
+
+// ---- CholeskyQR without a triangular solve ----------------------------------------------
+// The Cholesky elimination leaves L_G^{-1} (strict lower triangle of the RL buffer, unit
+// diagonal implicit) and D, with R^{-1} = L_G^{-T} D^{-1/2}.  These policies build
+// L_G^{-1} panel by panel and apply R^{-1}.
+
+// L_G^{-1}[k1+m][j] = C_in - sum_c L21[m][c] * U(c, j), j < k1, where U = the panel rows of
+// L_G^{-1} (written by the panel kernel) with the unit diagonal, and C_in = 0 for the
+// panel's own columns (identity block, i != j).
+struct LinvTrailArgs {
+  int n, k0, k1, ldw;
+  float* RL;
+  const float* W;  // raw L21, rows [k1, n)
+};
+__device__ __forceinline__ float linv_u(const float* RL, int n, int r, int j) {
+  return (j < r) ? RL[(int64_t)r * n + j] : (j == r ? 1.f : 0.f);
+}
+struct LinvTrail {
+  using Args = LinvTrailArgs;
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) {
+    M = a.n - a.k1;
+    N = a.k1;
+    K = a.k1 - a.k0;
+  }
+  __device__ static bool live(int, int) { return true; }
+  __device__ static float ldA(const Args& a, int64_t b, int k, int m) {
+    return a.W[((int64_t)b * a.n + a.k1 + m) * a.ldw + k];
+  }
+  __device__ static float ldB(const Args& a, int64_t b, int k, int j) {
+    return linv_u(a.RL + mat_off(b, a.n), a.n, a.k0 + k, j);
+  }
+  __device__ static void epi(const Args& a, int64_t b, int m, int j, float v) {
+    float* p = a.RL + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + j;
+    *p = ((j < a.k0) ? *p : 0.f) - v;
+  }
+};
+
+// R^{-1}(k, j) of one CholeskyQR pass, and its use:
+//   pass 1: Q[m][j] = sum_k X[m][k] R^{-1}[k][j]
+//   pass 2: Q[m][j] = X[m][j] - sum_k X[m][k] F[k][j],  F = I - R^{-1}  (small: the tensor
+//           cores / accumulators only see the correction, float32 does the subtraction)
+struct QApplyArgs {
+  int n;
+  int pass2;
+  const float* X;
+  const float* RL;
+  const float* D;
+  float* Q;
+  int* info;
+};
+__device__ __forceinline__ float rinv_entry(const QApplyArgs& a, int64_t b, int k, int j) {
+  if (k > j) return 0.f;
+  const float rs = 1.f / sqrtf(a.D[b * a.n + j]);
+  if (k == j) return a.pass2 ? (1.f - rs) : rs;
+  const float l = a.RL[mat_off(b, a.n) + (int64_t)j * a.n + k];
+  return a.pass2 ? -(l * rs) : l * rs;
+}
+struct QApply {
+  using Args = QApplyArgs;
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) { M = N = K = a.n; }
+  __device__ static bool live(int, int) { return true; }
+  __device__ static float ldA(const Args& a, int64_t b, int k, int m) {
+    return a.X[mat_off(b, a.n) + (int64_t)m * a.n + k];
+  }
+  __device__ static float ldB(const Args& a, int64_t b, int k, int j) {
+    return rinv_entry(a, b, k, j);
+  }
+  __device__ static void epi(const Args& a, int64_t b, int m, int j, float v) {
+    const int64_t o = mat_off(b, a.n) + (int64_t)m * a.n + j;
+    a.Q[o] = a.pass2 ? a.X[o] - v : v;
+  }
+};
+
+// G[j][j] = sum_k X[k][j]^2 in float32 (fixed order): exact diagonals for the second Gram.
+__global__ void __launch_bounds__(256) colnorm2_kernel(const float* __restrict__ X,
+                                                       float* __restrict__ G, int n) {
+  const int64_t b = blockIdx.y;
+  const int j = blockIdx.x * 256 + threadIdx.x;
+  if (j >= n) return;
+  const float* x = X + mat_off(b, n) + j;
+  float acc = 0.f;
+  for (int k = 0; k < n; ++k) {
+    const float v = x[(int64_t)k * n];
+    acc = fmaf(v, v, acc);
+  }
+  G[mat_off(b, n) + (int64_t)j * n + j] = acc;
+}
+
+}  // namespace qrb

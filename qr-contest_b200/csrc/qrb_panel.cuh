@@ -7,9 +7,12 @@
 //              HBM: the trailing block is kept "compact" (live rows at [k0,n) in current order)
 //              and the unit-lower factor is written in ORIGINAL row order, i.e. the kernel
 //              emits P*L directly -- the frame Q = P*Q_L (:81) then needs no permutation.
-//   PM_CHOL  : unpivoted LU of the jittered Gram G + mu*I (:74-76), emitting the upper
-//              Cholesky factor R = D^{1/2} L^T row block by row block.  Only the lower
-//              triangle of G is read (the diagonal block is mirrored in shared memory).
+//   PM_CHOL  : unpivoted LU of the jittered Gram G + mu*I (:74-76) = L_G D L_G^T, emitting
+//              the upper Cholesky rows R = D^{1/2} L_G^T (upper triangle of the R buffer),
+//              the pivots D, the raw multipliers L21 (for the trailing updates), and the
+//              panel rows of L_G^{-1} (strict lower triangle of the same buffer), so that
+//              R^{-1} = L_G^{-T} D^{-1/2} is available without a triangular solve.  Only the
+//              lower triangle of G is read (the diagonal block is mirrored in shared memory).
 //   PM_CHART : the chart (:144-162): sign rule s_k = +1 iff |1-d| >= |1+d|, pivot 1 + |d|,
 //              multipliers Y[i,k] = -s_k M[i,k] / piv, written straight into H's strict
 //              lower triangle; tau_k = 2 / (1 + sum_{i>k} Y[i,k]^2) (:192).
@@ -33,7 +36,9 @@ struct PanelArgs {
   int* srcmap;       // PIVOT: [b][n] out: new row -> old absolute row in src
   float* W;          // PIVOT/CHART: [b][n][ldw] out, rows [k0+w, n)
   float* L;          // PIVOT: [b][n][n] out, P*L (original row order)
-  float* R;          // CHOL: [b][n][n] out, upper rows [k0, k0+w)
+  float* R;          // CHOL: [b][n][n] out, upper rows [k0, k0+w) of R; strict lower rows
+                     //       [k0, k0+w) of L_G^{-1} (columns < row), read back for k0 > 0
+  float* D;          // CHOL: [b][n] out, pivots d_k (G = L_G D L_G^T)
   float* mu;         // CHOL: [b] jitter, computed when k0 == 0
   void* H;           // CHART: [b][n][n] out (output dtype), strict lower part
   void* tau;         // CHART: [b][n] out (output dtype)
@@ -209,6 +214,28 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
       float* Rrow = R + (int64_t)(k0 + c) * n + k0;
       for (int p = c + tid; p < m; p += 256)
         Rrow[p] = (p == c) ? sd : sd * P[p * ldp + c];
+    }
+    for (int c = tid; c < w; c += 256) a.D[b * n + k0 + c] = dpiv[c];
+    // panel rows of L_G^{-1}: rows [k0, k0+w) = L11^{-1} [ Linv(rows, 0:k0) | I_w ]
+    for (int j = tid; j < k0 + w; j += 256) {
+      float x[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        if (i < w) {
+          float v = (j < k0) ? R[(int64_t)(k0 + i) * n + j] : ((j - k0 == i) ? 1.f : 0.f);
+#pragma unroll
+          for (int l = 0; l < 32; ++l)
+            if (l < i) v = fmaf(-P[i * ldp + l], x[l], v);
+          x[i] = v;
+          if (j < k0 + i) R[(int64_t)(k0 + i) * n + j] = v;
+        }
+      }
+    }
+    // raw multipliers L21 for the trailing updates of L_G^{-1}
+    if (k0 + w < n) {
+      float* W = a.W + (int64_t)b * n * a.ldw;
+      for (int p = w + warp; p < m; p += 8)
+        for (int c = lane; c < w; c += 32) W[(int64_t)(k0 + p) * a.ldw + c] = P[p * ldp + c];
     }
   } else {  // PM_CHART
     TOut* H = reinterpret_cast<TOut*>(a.H) + mat_off(b, n);

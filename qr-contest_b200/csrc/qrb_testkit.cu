@@ -1,0 +1,93 @@
+// qrb200 test kit: single-stage entry points for the GPU unit tests (not part of the
+// product ABI).  Each runs one GEMM-shaped stage with either the SIMT tiles (tc = 0) or the
+// tcgen05 3xTF32 tiles (tc = 1) on float32 data, so the tests can compare both against a
+// float64 product of the same operands.
+#include "qrb_common.cuh"
+#include "qrb_gemm_simt.cuh"
+#include "qrb_tc_ops.cuh"
+
+using namespace qrb;
+
+static dim3 g64(int M, int N, int64_t b) { return dim3((N + 63) / 64, (M + 63) / 64, (unsigned)b); }
+static dim3 g128(int M, int N, int64_t b) { return dim3((N + 127) / 128, (M + 127) / 128, (unsigned)b); }
+constexpr int kSm = tc::SmemLayout<128>::TOTAL;
+
+template <class Pb>
+static int prep() {
+  return (int)cudaFuncSetAttribute(tc::tc_gemm_kernel<Pb, 128>,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize, kSm);
+}
+
+extern "C" {
+
+int qrbt_gram(const float* X, float* G, int* info, int64_t batch, int n, int use_tc, void* st) {
+  cudaStream_t s = (cudaStream_t)st;
+  if (use_tc) {
+    if (int e = prep<tc::GramTC>()) return e;
+    tc::tc_gemm_kernel<tc::GramTC, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(
+        tc::GramTCArgs{n, X, G, info});
+  } else {
+    simt_gemm_kernel<Gram><<<g64(n, n, batch), 256, 0, s>>>(GramArgs{n, X, G});
+  }
+  return (int)cudaGetLastError();
+}
+
+int qrbt_trailw(const float* Cold, float* Cnew, const float* W, const int* srcmap, int* info,
+                int64_t batch, int n, int k0, int k1, int ldw, int use_tc, void* st) {
+  cudaStream_t s = (cudaStream_t)st;
+  if (use_tc) {
+    if (int e = prep<tc::TrailWTC<float>>()) return e;
+    tc::tc_gemm_kernel<tc::TrailWTC<float>, 128><<<g128(n - k1, n - k1, batch), tc::NTHREADS,
+                                                   kSm, s>>>(
+        tc::TrailWTCArgs{n, k0, k1, ldw, Cold, Cnew, W, srcmap, info});
+  } else {
+    simt_gemm_kernel<TrailW<float>><<<g64(n - k1, n - k1, batch), 256, 0, s>>>(
+        TrailWArgs{n, k0, k1, ldw, Cold, Cnew, W, srcmap});
+  }
+  return (int)cudaGetLastError();
+}
+
+int qrbt_syrk(float* G, const float* R, int* info, int64_t batch, int n, int k0, int k1,
+              int use_tc, void* st) {
+  cudaStream_t s = (cudaStream_t)st;
+  if (use_tc) {
+    if (int e = prep<tc::SyrkTC>()) return e;
+    tc::tc_gemm_kernel<tc::SyrkTC, 128><<<g128(n - k1, n - k1, batch), tc::NTHREADS, kSm, s>>>(
+        tc::SyrkTCArgs{n, k0, k1, G, R, info});
+  } else {
+    simt_gemm_kernel<TrailSyrk><<<g64(n - k1, n - k1, batch), 256, 0, s>>>(
+        TrailSyrkArgs{n, k0, k1, G, R});
+  }
+  return (int)cudaGetLastError();
+}
+
+int qrbt_closure(const float* Q, const float* A, const float* sgn, float* H, int* info,
+                 int64_t batch, int n, int use_tc, void* st) {
+  cudaStream_t s = (cudaStream_t)st;
+  if (use_tc) {
+    if (int e = prep<tc::ClosureTC<float>>()) return e;
+    tc::tc_gemm_kernel<tc::ClosureTC<float>, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(
+        tc::ClosureTCArgs{n, Q, A, sgn, H, info});
+  } else {
+    simt_gemm_kernel<Closure<float>><<<g64(n, n, batch), 256, 0, s>>>(
+        ClosureArgs{n, Q, A, sgn, H});
+  }
+  return (int)cudaGetLastError();
+}
+
+// Q = X R^{-1} (pass2 = 0) or X - X (I - R^{-1}) (pass2 = 1), R^{-1}[k][j] = RL[j][k] / sqrt(D[j])
+// for k < j and 1 / sqrt(D[j]) on the diagonal.
+int qrbt_qapply(const float* X, const float* RL, const float* D, float* Q, int* info,
+                int64_t batch, int n, int pass2, int use_tc, void* st) {
+  cudaStream_t s = (cudaStream_t)st;
+  const QApplyArgs qa{n, pass2, X, RL, D, Q, info};
+  if (use_tc) {
+    if (int e = prep<tc::QApplyTC>()) return e;
+    tc::tc_gemm_kernel<tc::QApplyTC, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(qa);
+  } else {
+    simt_gemm_kernel<QApply><<<g64(n, n, batch), 256, 0, s>>>(qa);
+  }
+  return (int)cudaGetLastError();
+}
+
+}  // extern "C"

@@ -25,6 +25,10 @@ INFO_NONFINITE_INPUT = 1
 INFO_CHOL1_NOT_PD = 2
 INFO_CHOL2_NOT_PD = 4
 INFO_LU_ZERO_PIVOT = 8
+INFO_DEVICE_TIMEOUT = 16
+
+OPT_GEMM_PATH = 1
+GEMM_AUTO, GEMM_SIMT, GEMM_TC = 0, 1, 2
 
 # every symbol include/qrb200.h declares, with its ctypes signature
 SIGNATURES = {
@@ -47,6 +51,7 @@ SIGNATURES = {
     "qrb200_family_name": (ctypes.c_char_p, [ctypes.c_int32]),
     "qrb200_launch_count": (ctypes.c_longlong, []),
     "qrb200_last_cuda_error": (ctypes.c_char_p, []),
+    "qrb200_set_option": (ctypes.c_int, [ctypes.c_int32, ctypes.c_int64]),
     "qrb200_geqrf_batched_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
                                                     ctypes.c_void_p, ctypes.c_void_p,
                                                     ctypes.c_int64, ctypes.c_int32,
@@ -117,3 +122,10 @@ def geqrf_batched_timed(A_ptr, H_ptr, tau_ptr, info_ptr, batch, n, dtype, ws_ptr
     rc = lib().qrb200_geqrf_batched_timed(A_ptr, H_ptr, tau_ptr, info_ptr, int(batch), int(n),
                                           int(dtype), ws_ptr, int(ws_bytes), stream_ptr, buf)
     return rc, dict(zip(families(), [float(x) for x in buf]))
+
+
+def set_gemm_path(path: int) -> None:
+    """0 = automatic, 1 = SIMT tiles only, 2 = tcgen05 tiles whenever n % 4 == 0."""
+    rc = lib().qrb200_set_option(OPT_GEMM_PATH, int(path))
+    if rc != QRB200_OK:
+        raise QRB200Error(rc, "qrb200_set_option")

@@ -18,6 +18,7 @@ ROOT = PKG.parent                      # qr-contest_b200/
 CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 LIB = PKG / "libqrb200.so"
+TESTKIT = PKG / "libqrb200_testkit.so"   # single-stage entry points for the GPU unit tests
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
@@ -35,21 +36,24 @@ def sources():
     return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
 
 
-def up_to_date() -> bool:
-    if not LIB.exists():
+def up_to_date(target: Path) -> bool:
+    if not target.exists():
         return False
-    t = LIB.stat().st_mtime
+    t = target.stat().st_mtime
     return all(p.stat().st_mtime <= t for p in sources())
 
 
-def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
-    if not force and up_to_date():
-        return LIB
-    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-I", str(INCLUDE), "-o", str(LIB),
-           str(CSRC / "qrb_api.cu")]
+def _compile(src: Path, out: Path, verbose: bool, extra) -> None:
+    cmd = [nvcc(), *ARCH, *FLAGS, *extra, "-I", str(INCLUDE), "-o", str(out), str(src)]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
+
+
+def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
+    for src, out in ((CSRC / "qrb_api.cu", LIB), (CSRC / "qrb_testkit.cu", TESTKIT)):
+        if force or not up_to_date(out):
+            _compile(src, out, verbose, extra)
     return LIB
 
 
