@@ -15,6 +15,7 @@
 #include "qrb_gemm_simt.cuh"
 #include "qrb_panel.cuh"
 #include "qrb_tc_ops.cuh"
+#include "qrb_rankw.cuh"
 
 #include <atomic>
 #include <mutex>
@@ -92,7 +93,7 @@ static int pick_nb(int n) {
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
 
 struct Ws {
-  float *T0, *T1, *L, *R, *Q1, *W, *s, *mu, *D;
+  float *T0, *T1, *L, *R, *Q1, *W, *s, *mu, *D, *Wc, *Bp;
   int *orig, *srcmap;
 };
 
@@ -100,7 +101,7 @@ static size_t per_chunk_bytes(int64_t cb, int n, int nbmax) {
   const size_t nn = (size_t)n * n;
   size_t t = 0;
   t += 5 * align256(cb * nn * sizeof(float));
-  t += align256(cb * (size_t)n * nbmax * sizeof(float));
+  t += 3 * align256(cb * (size_t)n * nbmax * sizeof(float));  // W, Wc, Bp
   t += align256(cb * (size_t)n * sizeof(float));  // s
   t += align256(cb * sizeof(float));              // mu
   t += align256(cb * (size_t)n * sizeof(float));  // D
@@ -127,6 +128,8 @@ static Ws carve(void* base, int64_t cb, int n, int nbmax) {
   w.R = (float*)take(cb * nn * sizeof(float));
   w.Q1 = (float*)take(cb * nn * sizeof(float));
   w.W = (float*)take(cb * (size_t)n * nbmax * sizeof(float));
+  w.Wc = (float*)take(cb * (size_t)n * nbmax * sizeof(float));
+  w.Bp = (float*)take(cb * (size_t)n * nbmax * sizeof(float));
   w.s = (float*)take(cb * (size_t)n * sizeof(float));
   w.mu = (float*)take(cb * sizeof(float));
   w.D = (float*)take(cb * (size_t)n * sizeof(float));
@@ -138,6 +141,9 @@ static Ws carve(void* base, int64_t cb, int n, int nbmax) {
 static inline dim3 tiles_grid(int M, int N, int64_t cb) {
   return dim3((N + GT - 1) / GT, (M + GT - 1) / GT, (unsigned)cb);
 }
+static inline dim3 rw_grid(int M, int N, int64_t cb) {
+  return dim3((N + RW_N - 1) / RW_N, (M + RW_M - 1) / RW_M, (unsigned)cb);
+}
 
 // tcgen05 tiles need float4-aligned rows; small orders stay on the SIMT tiles.
 static inline bool use_tc(int n) {
@@ -145,6 +151,12 @@ static inline bool use_tc(int n) {
   if (p == 1) return false;
   if (p == 2) return (n & 3) == 0;
   return (n & 3) == 0 && n >= 128;
+}
+
+// Rank-w trailing updates stream on float4 rows (n % 4 == 0); QRB200_OPT_GEMM_PATH = 2 sends
+// the LU trailing update through the tcgen05 tiles instead (comparison runs).
+static inline bool use_rankw(int n) {
+  return (n & 3) == 0 && g_gemm_path.load(std::memory_order_relaxed) != 2;
 }
 
 template <class Pb>
@@ -221,6 +233,7 @@ static cudaError_t ensure_attrs() {
 static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, const Ws& ws,
                         int* info, int info_bit, cudaStream_t st, Prof* prof) {
   const bool tcp = use_tc(n);
+  const bool rw = use_rankw(n);
   const bool pass2 = (info_bit == INFO_CHOL2_NOT_PD);
   QRB_LAUNCH(prof, F_GRAM,
              if (tcp) tc::tc_gemm_kernel<tc::GramTC, 128><<<tc_grid(n, n, cb), tc::NTHREADS,
@@ -235,23 +248,23 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
     const int w = (n - k0 < nb) ? n - k0 : nb;
     PanelArgs pa{};
     pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
-    pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = ws.W; pa.mu = ws.mu; pa.info = info;
-    pa.info_bit = info_bit;
+    pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = ws.W; pa.Wc = ws.Wc; pa.Bp = ws.Bp;
+    pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
     QRB_LAUNCH(prof, F_CHOL_PANEL,
                panel_kernel<PM_CHOL, float, float>
                <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
     const int k1 = k0 + w;
-    if (k1 < n) {
+    if (k1 < n)
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 if (tcp) tc::tc_gemm_kernel<tc::SyrkTC, 128>
-                     <<<tc_grid(n - k1, n - k1, cb), tc::NTHREADS, kTcSmem, st>>>(
-                         tc::SyrkTCArgs{n, k0, k1, ws.T0, ws.R, info});
+                 if (rw) rankw_kernel<RWSyrk><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                     RWSyrkArgs{n, k0, k1, nb, ws.T0, ws.R, ws.Wc});
                  else simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
                      TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
-      QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k1, k1, cb), 256, 0, st>>>(
-                     LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W}));
-    }
+    QRB_LAUNCH(prof, F_CHOL_TRAIL,
+               if (rw) rankw_kernel<RWLinv><<<rw_grid(n - k0, k1, cb), 256, 0, st>>>(
+                   RWLinvArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp});
+               else simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k0, k1, cb), 256, 0, st>>>(
+                   LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp}));
   }
   const QApplyArgs qa{n, pass2 ? 1 : 0, X, ws.R, ws.D, Q, info};
   QRB_LAUNCH(prof, F_QAPPLY,
@@ -265,6 +278,7 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
                              const Ws& ws, cudaStream_t st, Prof* prof) {
   const int nb = pick_nb(n);
   const bool tcp = use_tc(n);
+  const bool rw = use_rankw(n);  // streaming rank-w tiles for every trailing update
   cudaError_t e = cudaMemsetAsync(info, 0, cb * sizeof(int), st);
   if (e != cudaSuccess) return e;
 
@@ -290,8 +304,12 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
         const dim3 g = tiles_grid(n - k1, n - k1, cb);
         const tc::TrailWTCArgs tca{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap, info};
         const dim3 gt = tc_grid(n - k1, n - k1, cb);
+        const RWTrailArgs rwa{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap};
+        const dim3 gr = rw_grid(n - k1, n - k1, cb);
         QRB_LAUNCH(prof, F_LU_TRAIL,
-                   if (tcp && cur_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, 128>
+                   if (rw && cur_in) rankw_kernel<RWTrail<T>><<<gr, 256, 0, st>>>(rwa);
+                   else if (rw) rankw_kernel<RWTrail<float>><<<gr, 256, 0, st>>>(rwa);
+                   else if (tcp && cur_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, 128>
                        <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
                    else if (tcp) tc::tc_gemm_kernel<tc::TrailWTC<float>, 128>
                        <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
@@ -322,7 +340,9 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
     // and the 2^-21 products of 3xTF32 would push it below the tau >= 1 - 1e-6 gate.
     if (k1 < n)
       QRB_LAUNCH(prof, F_CHART_TRAIL,
-                 simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                 if (rw) rankw_kernel<RWTrail<float>><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                     RWTrailArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr});
+                 else simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
                      TrailWArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr}));
   }
   // ---- II: closure, H_upper = s * triu(Q^T A) ----

@@ -193,34 +193,37 @@ namespace qrb {
 // diagonal implicit) and D, with R^{-1} = L_G^{-T} D^{-1/2}.  These policies build
 // L_G^{-1} panel by panel and apply R^{-1}.
 
-// L_G^{-1}[k1+m][j] = C_in - sum_c L21[m][c] * U(c, j), j < k1, where U = the panel rows of
-// L_G^{-1} (written by the panel kernel) with the unit diagonal, and C_in = 0 for the
-// panel's own columns (identity block, i != j).
+// L_G^{-1} update of one Cholesky panel, scalar tiles (any n); same contract as RWLinv in
+// qrb_rankw.cuh: rows [k0, k1) get L11^{-1} B, rows [k1, n) get C_in - W B (j < k1), with
+// A rows = [L11^{-1}; W] and B = the panel rows of L_G^{-1} before the panel.
 struct LinvTrailArgs {
   int n, k0, k1, ldw;
   float* RL;
-  const float* W;  // raw L21, rows [k1, n)
+  const float* Wl;
+  const float* Bp;
 };
-__device__ __forceinline__ float linv_u(const float* RL, int n, int r, int j) {
-  return (j < r) ? RL[(int64_t)r * n + j] : (j == r ? 1.f : 0.f);
-}
 struct LinvTrail {
   using Args = LinvTrailArgs;
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
-    M = a.n - a.k1;
+    M = a.n - a.k0;
     N = a.k1;
     K = a.k1 - a.k0;
   }
   __device__ static bool live(int, int) { return true; }
   __device__ static float ldA(const Args& a, int64_t b, int k, int m) {
-    return a.W[((int64_t)b * a.n + a.k1 + m) * a.ldw + k];
+    return a.Wl[((int64_t)b * a.n + a.k0 + m) * a.ldw + k];
   }
   __device__ static float ldB(const Args& a, int64_t b, int k, int j) {
-    return linv_u(a.RL + mat_off(b, a.n), a.n, a.k0 + k, j);
+    return a.Bp[((int64_t)b * a.ldw + k) * a.n + j];
   }
   __device__ static void epi(const Args& a, int64_t b, int m, int j, float v) {
-    float* p = a.RL + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + j;
-    *p = ((j < a.k0) ? *p : 0.f) - v;
+    const int r = a.k0 + m;
+    float* p = a.RL + mat_off(b, a.n) + (int64_t)r * a.n + j;
+    if (r < a.k1) {
+      if (j < r) *p = v;
+    } else {
+      *p = ((j < a.k0) ? *p : 0.f) - v;
+    }
   }
 };
 

@@ -9,8 +9,9 @@
 //              emits P*L directly -- the frame Q = P*Q_L (:81) then needs no permutation.
 //   PM_CHOL  : unpivoted LU of the jittered Gram G + mu*I (:74-76) = L_G D L_G^T, emitting
 //              the upper Cholesky rows R = D^{1/2} L_G^T (upper triangle of the R buffer),
-//              the pivots D, the raw multipliers L21 (for the trailing updates), and the
-//              panel rows of L_G^{-1} (strict lower triangle of the same buffer), so that
+//              the pivots D, L21 D^{1/2} (Cholesky trailing update), and what the L_G^{-1}
+//              update needs (L11^{-1}, W = L21 L11^{-1}, the panel rows of L_G^{-1}); L_G^{-1}
+//              itself accumulates in the strict lower triangle of the R buffer, so that
 //              R^{-1} = L_G^{-T} D^{-1/2} is available without a triangular solve.  Only the
 //              lower triangle of G is read (the diagonal block is mirrored in shared memory).
 //   PM_CHART : the chart (:144-162): sign rule s_k = +1 iff |1-d| >= |1+d|, pivot 1 + |d|,
@@ -34,11 +35,14 @@ struct PanelArgs {
   const void* src;   // current trailing buffer: rows/cols [k0, n) valid (input dtype at k0 == 0)
   int* orig;         // PIVOT: [b][n] original row id of each current row
   int* srcmap;       // PIVOT: [b][n] out: new row -> old absolute row in src
-  float* W;          // PIVOT/CHART: [b][n][ldw] out, rows [k0+w, n)
+  float* W;          // [b][n][ldw] out, rows [k0+w, n): W; CHOL also rows [k0, k0+w): L11^{-1}
   float* L;          // PIVOT: [b][n][n] out, P*L (original row order)
   float* R;          // CHOL: [b][n][n] out, upper rows [k0, k0+w) of R; strict lower rows
                      //       [k0, k0+w) of L_G^{-1} (columns < row), read back for k0 > 0
   float* D;          // CHOL: [b][n] out, pivots d_k (G = L_G D L_G^T)
+  float* Wc;         // CHOL: [b][n][ldw] out, rows [k0+w, n): L21 D^{1/2}
+  float* Bp;         // CHOL: [b][ldw][n] out, rows of L_G^{-1} [k0, k0+w) before the panel
+                     //       (columns < k0+w, identity block included)
   float* mu;         // CHOL: [b] jitter, computed when k0 == 0
   void* H;           // CHART: [b][n][n] out (output dtype), strict lower part
   void* tau;         // CHART: [b][n] out (output dtype)
@@ -216,26 +220,36 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
         Rrow[p] = (p == c) ? sd : sd * P[p * ldp + c];
     }
     for (int c = tid; c < w; c += 256) a.D[b * n + k0 + c] = dpiv[c];
-    // panel rows of L_G^{-1}: rows [k0, k0+w) = L11^{-1} [ Linv(rows, 0:k0) | I_w ]
-    for (int j = tid; j < k0 + w; j += 256) {
+    // raw panel rows of L_G^{-1} before this panel (identity block included), columns < k1
+    for (int c = warp; c < w; c += 8) {
+      float* bp = a.Bp + ((int64_t)b * a.ldw + c) * n;
+      const float* rl = R + (int64_t)(k0 + c) * n;
+      for (int j = lane; j < k0 + w; j += 32)
+        bp[j] = (j < k0) ? rl[j] : ((j == k0 + c) ? 1.f : 0.f);
+    }
+    // L11^{-1} (unit lower) into rows [k0, k0+w) of the W buffer
+    if (tid < w) {
+      const int c = tid;
+      float* Wl = a.W + (int64_t)b * n * a.ldw;
       float x[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        if (i < w) {
-          float v = (j < k0) ? R[(int64_t)(k0 + i) * n + j] : ((j - k0 == i) ? 1.f : 0.f);
+        float v = (i == c) ? 1.f : 0.f;
+        if (i > c && i < w) {
 #pragma unroll
           for (int l = 0; l < 32; ++l)
-            if (l < i) v = fmaf(-P[i * ldp + l], x[l], v);
-          x[i] = v;
-          if (j < k0 + i) R[(int64_t)(k0 + i) * n + j] = v;
+            if (l >= c && l < i) v = fmaf(-P[i * ldp + l], x[l], v);
         }
+        x[i] = v;
+        if (i < w) Wl[(int64_t)(k0 + i) * a.ldw + c] = v;
       }
     }
-    // raw multipliers L21 for the trailing updates of L_G^{-1}
+    // L21 D^{1/2} (rows [k0+w, n)) for the Cholesky trailing update
     if (k0 + w < n) {
-      float* W = a.W + (int64_t)b * n * a.ldw;
+      float* Wc = a.Wc + (int64_t)b * n * a.ldw;
       for (int p = w + warp; p < m; p += 8)
-        for (int c = lane; c < w; c += 32) W[(int64_t)(k0 + p) * a.ldw + c] = P[p * ldp + c];
+        for (int c = lane; c < w; c += 32)
+          Wc[(int64_t)(k0 + p) * a.ldw + c] = P[p * ldp + c] * sqrtf(dpiv[c]);
     }
   } else {  // PM_CHART
     TOut* H = reinterpret_cast<TOut*>(a.H) + mat_off(b, n);
@@ -258,8 +272,8 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
     }
   }
 
-  // ---- W = L21 * L11^{-1} for the trailing update (PIVOT and CHART) ----
-  if (MODE != PM_CHOL && k0 + w < n) {
+  // ---- W = L21 * L11^{-1} for the trailing update (PIVOT, CHART; CHOL: of L_G^{-1}) ----
+  if (k0 + w < n) {
     __syncthreads();
     for (int p = w + tid; p < m; p += 256) {
       float* row = P + p * ldp;

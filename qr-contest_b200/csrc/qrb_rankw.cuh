@@ -1,0 +1,215 @@
+// qrb200 -- rank-w trailing updates (w <= 32) as one memory-streaming pass per panel.
+//
+// Every blocked elimination of the pipeline ends a panel with C' = C - A B where K = w is
+// the panel width: the LU and chart trailing updates (reflection_no_reflectors.py:66 via
+// getrf, :174), the Cholesky trailing update (:76 via potrf) and the L_G^{-1} update of the
+// CholeskyQR passes.  With K = 32 the update does 64 flops per 8 bytes of C streamed, so it
+// is bound by HBM bandwidth, not arithmetic: the kernel is built for streaming -- float4
+// loads of whole rows, the gathered row pointer resolved once per row, the K-slice of A
+// and B staged once in shared memory, and a 64 x 128 tile per CTA (4 x 8 outputs per
+// thread) so each thread keeps 8 independent row segments in flight.
+//
+// Policy Pb supplies: Args; dims(a, M, N, K); live(a, m0, n0);
+//   a_ptr(a, b, m)  -> const float*  row m of A (K contiguous floats, 16-byte aligned)
+//   b_ptr(a, b, k)  -> const TB*     row k of B (B(k, j) = p[j], j < N, 16-byte aligned)
+//   epi4(a, b, m, j, acc[4])         columns j .. j+3 of row m (j % 4 == 0, j + 3 < N)
+// Requires n % 4 == 0 (callers fall back to the scalar tiles otherwise).
+#pragma once
+#include "qrb_common.cuh"
+
+namespace qrb {
+
+constexpr int RW_M = 64, RW_N = 128, RW_K = 32;
+
+template <typename T>
+__device__ __forceinline__ float4 ld4v(const T* p) {
+  if constexpr (sizeof(T) == 4) {
+    return __ldg(reinterpret_cast<const float4*>(p));
+  } else {
+    const uint2 t = __ldg(reinterpret_cast<const uint2*>(p));
+    const T* h = reinterpret_cast<const T*>(&t);
+    return make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+  }
+}
+// non-cached variant for buffers the same kernel also writes
+__device__ __forceinline__ float4 ld4rw(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+__device__ __forceinline__ void st4(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+
+template <class Pb>
+__global__ void __launch_bounds__(256) rankw_kernel(typename Pb::Args a) {
+  __shared__ __align__(16) float As[RW_K][RW_M + 4];
+  __shared__ __align__(16) float Bs[RW_K][RW_N + 4];
+  const int64_t b = blockIdx.z;
+  const int m0 = blockIdx.y * RW_M, n0 = blockIdx.x * RW_N;
+  int M, N, K;
+  Pb::dims(a, M, N, K);
+  if (m0 >= M || n0 >= N || !Pb::live(a, m0, n0)) return;
+  const int tid = threadIdx.x;
+
+  // A: 64 rows x K (<= 32) -> As[k][m]
+#pragma unroll
+  for (int rep = 0; rep < 2; ++rep) {
+    const int mm = (tid >> 3) + 32 * rep, kc = tid & 7;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (m0 + mm < M && 4 * kc < K) v = __ldg(reinterpret_cast<const float4*>(Pb::a_ptr(a, b, m0 + mm) + 4 * kc));
+    As[4 * kc + 0][mm] = v.x;
+    As[4 * kc + 1][mm] = v.y;
+    As[4 * kc + 2][mm] = v.z;
+    As[4 * kc + 3][mm] = v.w;
+  }
+  // B: K rows x 128 columns -> Bs[k][j]
+#pragma unroll
+  for (int rep = 0; rep < 4; ++rep) {
+    const int k = (tid >> 5) + 8 * rep, c4 = (tid & 31) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k < K && n0 + c4 < N) v = ld4v(Pb::b_ptr(a, b, k) + n0 + c4);
+    st4(&Bs[k][c4], v);
+  }
+  __syncthreads();
+
+  const int tn = tid & 15, tm = tid >> 4;
+  float acc[4][8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const float4 av = *reinterpret_cast<const float4*>(&As[k][tm * 4]);
+    const float4 b0 = *reinterpret_cast<const float4*>(&Bs[k][tn * 8]);
+    const float4 b1 = *reinterpret_cast<const float4*>(&Bs[k][tn * 8 + 4]);
+    const float ar[4] = {av.x, av.y, av.z, av.w};
+    const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + tm * 4 + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = n0 + tn * 8 + 4 * h;
+      if (j < N) Pb::epi4(a, b, m, j, &acc[i][4 * h]);
+    }
+  }
+}
+
+// ---- LU / chart trailing update: C'[k1+m][k1+j] = C[src(k1+m)][k1+j] - (W C[src(k0:k1)])
+struct RWTrailArgs {
+  int n, k0, k1, ldw;
+  const void* Cold;
+  float* Cnew;
+  const float* W;
+  const int* srcmap;  // nullptr -> identity
+};
+template <typename T>
+struct RWTrail {
+  using Args = RWTrailArgs;
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) {
+    M = N = a.n - a.k1;
+    K = a.k1 - a.k0;
+  }
+  __device__ static bool live(const Args&, int, int) { return true; }
+  __device__ static int srow(const Args& a, int64_t b, int r) {
+    return a.srcmap ? a.srcmap[b * a.n + r] : r;
+  }
+  __device__ static const float* a_ptr(const Args& a, int64_t b, int m) {
+    return a.W + ((int64_t)b * a.n + a.k1 + m) * a.ldw;
+  }
+  __device__ static const T* b_ptr(const Args& a, int64_t b, int k) {
+    return reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
+           (int64_t)srow(a, b, a.k0 + k) * a.n + a.k1;
+  }
+  __device__ static void epi4(const Args& a, int64_t b, int m, int j, const float* v) {
+    const T* c = reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
+                 (int64_t)srow(a, b, a.k1 + m) * a.n + a.k1 + j;
+    float4 x = (reinterpret_cast<const void*>(a.Cold) == reinterpret_cast<const void*>(a.Cnew))
+                   ? ld4rw(reinterpret_cast<const float*>(c))
+                   : ld4v(c);
+    x.x -= v[0]; x.y -= v[1]; x.z -= v[2]; x.w -= v[3];
+    st4(a.Cnew + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j, x);
+  }
+};
+
+// ---- Cholesky trailing update on the lower triangle: G22 -= (L21 D^{1/2}) R12 -----------
+struct RWSyrkArgs {
+  int n, k0, k1, ldw;
+  float* G;
+  const float* R;   // rows [k0, k1): R12 = D^{1/2} L21^T
+  const float* Wc;  // rows [k1, n): L21 D^{1/2}
+};
+struct RWSyrk {
+  using Args = RWSyrkArgs;
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) {
+    M = N = a.n - a.k1;
+    K = a.k1 - a.k0;
+  }
+  __device__ static bool live(const Args&, int m0, int n0) { return n0 < m0 + RW_M; }
+  __device__ static const float* a_ptr(const Args& a, int64_t b, int m) {
+    return a.Wc + ((int64_t)b * a.n + a.k1 + m) * a.ldw;
+  }
+  __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
+    return a.R + mat_off(b, a.n) + (int64_t)(a.k0 + k) * a.n + a.k1;
+  }
+  __device__ static void epi4(const Args& a, int64_t b, int m, int j, const float* v) {
+    if (j > m + 3) return;  // strictly upper 4-block: never read
+    float* g = a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j;
+    float4 x = ld4rw(g);
+    x.x -= v[0]; x.y -= v[1]; x.z -= v[2]; x.w -= v[3];
+    st4(g, x);
+  }
+};
+
+// ---- L_G^{-1} update of one Cholesky panel (strict lower triangle of RL) -----------------
+//   rows r in [k0, k1):  Linv[r][j] = (L11^{-1} B)[r - k0][j],           j < r
+//   rows r in [k1, n):   Linv[r][j] = C_in[r][j] - (W B)[r - k1][j],       j < k1
+// with B = the panel rows of L_G^{-1} before the panel (Bp, identity block included),
+// A rows = [L11^{-1}; W] (W = L21 L11^{-1}), C_in = Linv[r][j] for j < k0 and 0 on the
+// panel's own columns.  B lives in its own buffer, so the panel rows can be overwritten.
+struct RWLinvArgs {
+  int n, k0, k1, ldw;
+  float* RL;
+  const float* Wl;  // rows [k0, n): L11^{-1} then W
+  const float* Bp;  // [ldw][n] per matrix: raw panel rows, columns [0, k1)
+};
+struct RWLinv {
+  using Args = RWLinvArgs;
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) {
+    M = a.n - a.k0;
+    N = a.k1;
+    K = a.k1 - a.k0;
+  }
+  __device__ static bool live(const Args&, int, int) { return true; }
+  __device__ static const float* a_ptr(const Args& a, int64_t b, int m) {
+    return a.Wl + ((int64_t)b * a.n + a.k0 + m) * a.ldw;
+  }
+  __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
+    return a.Bp + ((int64_t)b * a.ldw + k) * a.n;
+  }
+  __device__ static void epi4(const Args& a, int64_t b, int m, int j, const float* v) {
+    const int r = a.k0 + m;
+    float* p = a.RL + mat_off(b, a.n) + (int64_t)r * a.n + j;
+    if (r < a.k1) {
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        if (j + t < r) p[t] = v[t];
+    } else {
+      float4 x = (j + 3 < a.k0) ? ld4rw(p) : make_float4(0.f, 0.f, 0.f, 0.f);
+      if (j < a.k0 && j + 3 >= a.k0) {  // straddles k0 (k0 % 4 == 0 makes this impossible)
+        const float t[4] = {p[0], p[1], p[2], p[3]};
+        x.x = (j + 0 < a.k0) ? t[0] : 0.f;
+        x.y = (j + 1 < a.k0) ? t[1] : 0.f;
+        x.z = (j + 2 < a.k0) ? t[2] : 0.f;
+        x.w = (j + 3 < a.k0) ? t[3] : 0.f;
+      }
+      x.x -= v[0]; x.y -= v[1]; x.z -= v[2]; x.w -= v[3];
+      st4(p, x);
+    }
+  }
+};
+
+}  // namespace qrb
