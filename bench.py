@@ -48,6 +48,9 @@ def parse():
     p.add_argument("--cpu-sample", type=int, default=16, help="matrices per class (CPU leg)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--profile-run", action="store_true",
+                   help="one warm-up call and one measured call of the library, nothing else "
+                        "(the command the ncu summaries under profiles/ are taken on)")
     return p.parse_args()
 
 
@@ -263,6 +266,14 @@ def run_qrb(args):
 
     def step():
         return qrb200.geqrf(A, workspace=ws)
+
+    if args.profile_run:
+        step()
+        torch.cuda.synchronize(dev)
+        step()
+        torch.cuda.synchronize(dev)
+        print(json.dumps({"profile_run": True, "launches_per_call": _lib.launch_count() // 2}))
+        return
 
     for _ in range(max(3, args.warmup)):
         H, tau, info = step()

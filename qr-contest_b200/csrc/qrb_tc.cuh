@@ -152,7 +152,9 @@ __device__ __forceinline__ void put4x4(char* hi, char* lo, int r0, int kchunk,
 //   krange(a, m0, n0, kb, ke) (k range the tile reduces over);
 //   A_ALONG_K / B_ALONG_K : the global source of A(m,k) / B(k,j) is contiguous along k
 //   loadA(a, b, m0, k0, v[4][4]) : v[i][kk] = A(m0+i, k0+kk), zero outside
-//   loadB(a, b, j0, k0, v[4][4]) : v[i][kk] = B(k0+kk, j0+i), zero outside
+//   loadB(a, b, j0, k0, v[4][4]) : v[i][kk] = B(k0+kk, j0+i), zero outside (raw loads)
+//   fixB(a, b, j0, k0, v[4][4])  : elementwise transform of a fetched B block, applied when
+//                                  it is written to shared memory (keeps loads in flight)
 //   store(a, b, m, j0, v[32], M, N) : row m, columns j0 .. j0+31 of the result
 //   info(a, b) : int* of the matrix's status word
 template <int BN>
@@ -200,23 +202,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_gemm_kernel(typename Pb::Args 
   auto stageB_hi = [&](int s) { return sm + s * L::STAGE + 2 * L::A_BYTES; };
   auto stageB_lo = [&](int s) { return sm + s * L::STAGE + 2 * L::A_BYTES + L::B_BYTES; };
 
-  auto load_stage = [&](int s, int k0) {
-    {  // A: 128 rows x 32 k = 256 micro-blocks
-      int mb, kc;
-      if (Pb::A_ALONG_K) { mb = tid >> 3; kc = tid & 7; }
-      else { mb = tid & 31; kc = tid >> 5; }
-      float v[4][4];
-      Pb::loadA(a, b, m0 + 4 * mb, k0 + 4 * kc, v);
-      put4x4(stageA_hi(s), stageA_lo(s), 4 * mb, kc, v);
-    }
-    constexpr int NB = BN * BK / 16;  // B micro-blocks
+  // Loader: each thread owns one 4x4 micro-block of A and (if tid < NB) one of B per stage.
+  // Global loads for stage it+2 are issued into registers while the MMAs of stage it run;
+  // they are split and written to shared memory only once that buffer is free again.
+  constexpr int NB = BN * BK / 16;  // B micro-blocks
+  int a_mb, a_kc, b_jb, b_kc;
+  if (Pb::A_ALONG_K) { a_mb = tid >> 3; a_kc = tid & 7; }
+  else { a_mb = tid & 31; a_kc = tid >> 5; }
+  if (Pb::B_ALONG_K) { b_jb = tid >> 3; b_kc = tid & 7; }
+  else { b_jb = tid % (BN / 4); b_kc = tid / (BN / 4); }
+  float va[4][4], vb[4][4];
+  auto fetch = [&](int k0) {
+    Pb::loadA(a, b, m0 + 4 * a_mb, k0 + 4 * a_kc, va);
+    if (tid < NB) Pb::loadB(a, b, n0 + 4 * b_jb, k0 + 4 * b_kc, vb);
+  };
+  auto put = [&](int s, int k0) {
+    put4x4(stageA_hi(s), stageA_lo(s), 4 * a_mb, a_kc, va);
     if (tid < NB) {
-      int jb, kc;
-      if (Pb::B_ALONG_K) { jb = tid >> 3; kc = tid & 7; }
-      else { jb = tid % (BN / 4); kc = tid / (BN / 4); }
-      float v[4][4];
-      Pb::loadB(a, b, n0 + 4 * jb, k0 + 4 * kc, v);
-      put4x4(stageB_hi(s), stageB_lo(s), 4 * jb, kc, v);
+      Pb::fixB(a, b, n0 + 4 * b_jb, k0 + 4 * b_kc, vb);
+      put4x4(stageB_hi(s), stageB_lo(s), 4 * b_jb, b_kc, vb);
     }
     fence_async_smem();
   };
@@ -226,7 +230,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_gemm_kernel(typename Pb::Args 
   bool ok = true;
   uint32_t phasebits = 0;  // bit s = parity of the next wait on bars[s]
 
-  if (nk > 0) load_stage(0, kb);
+  if (nk > 0) {
+    fetch(kb);
+    put(0, kb);
+    if (nk > 1) fetch(kb + BK);
+  }
   __syncthreads();
   for (int it = 0; it < nk; ++it) {
     const int s = it & 1;
@@ -252,7 +260,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_gemm_kernel(typename Pb::Args 
         if (!mbar_wait(&bars[s2], (phasebits >> s2) & 1)) ok = false;
         phasebits ^= 1u << s2;
       }
-      if (ok) load_stage(s2, kb + (it + 1) * BK);
+      if (ok) put(s2, kb + (it + 1) * BK);
+      if (it + 2 < nk) fetch(kb + (it + 2) * BK);
       __syncthreads();
     }
   }

@@ -98,6 +98,7 @@ struct GramTC {
     st_row32(a.G + mat_off(b, a.n) + (int64_t)m * a.n + j0, v, N - j0, (a.n & 3) == 0);
   }
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
+  __device__ static void fixB(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 
 // ---------------------------------------------------------------------------------------
@@ -135,6 +136,7 @@ struct ClosureTC {
     }
   }
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
+  __device__ static void fixB(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 
 // ---------------------------------------------------------------------------------------
@@ -195,6 +197,7 @@ struct TrailWTC {
     sub_row32(C, D, v, N - j0, ((a.n & 3) == 0) && ((a.k1 & 3) == 0));
   }
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
+  __device__ static void fixB(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 
 // ---------------------------------------------------------------------------------------
@@ -230,6 +233,7 @@ struct SyrkTC {
     sub_row32(g, g, v, N - j0, ((a.n & 3) == 0) && ((a.k1 & 3) == 0));
   }
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
+  __device__ static void fixB(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 
 // ---------------------------------------------------------------------------------------
@@ -262,21 +266,26 @@ struct QApplyTC {
     for (int i = 0; i < 4; ++i) {
       const int j = j0 + i;
       float o[4] = {0.f, 0.f, 0.f, 0.f};
-      if (j < a.n && k0 <= j) {
-        ld4(RL + (int64_t)j * a.n + k0, clamp4(a.n - k0), true, o);
-        const float rs = 1.f / sqrtf(a.D[b * a.n + j]);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const int k = k0 + kk;
-          float r;
-          if (k < j) r = a.pass2 ? -(o[kk] * rs) : o[kk] * rs;
-          else if (k == j) r = a.pass2 ? (1.f - rs) : rs;
-          else r = 0.f;
-          o[kk] = r;
-        }
-      }
+      if (j < a.n && k0 <= j) ld4(RL + (int64_t)j * a.n + k0, clamp4(a.n - k0), true, o);
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk) v[i][kk] = o[kk];
+    }
+  }
+  // raw row j of the R buffer (strict lower = L_G^{-1}) -> R^{-1} or I - R^{-1}
+  __device__ static void fixB(const Args& a, int64_t b, int j0, int k0, float (&v)[4][4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = j0 + i;
+      const float rs = (j < a.n) ? 1.f / sqrtf(a.D[b * a.n + j]) : 0.f;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int k = k0 + kk;
+        float r;
+        if (j >= a.n || k > j) r = 0.f;
+        else if (k < j) r = a.pass2 ? -(v[i][kk] * rs) : v[i][kk] * rs;
+        else r = a.pass2 ? (1.f - rs) : rs;
+        v[i][kk] = r;
+      }
     }
   }
   __device__ static void store(const Args& a, int64_t b, int m, int j0, const float* v, int,
