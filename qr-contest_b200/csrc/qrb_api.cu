@@ -14,6 +14,7 @@
 #include "qrb_common.cuh"
 #include "qrb_gemm_simt.cuh"
 #include "qrb_panel.cuh"
+#include "qrb_panel_reg.cuh"
 #include "qrb_tc_ops.cuh"
 #include "qrb_rankw.cuh"
 
@@ -223,6 +224,16 @@ static cudaError_t ensure_attrs() {
   return e;
 }
 
+// Panels of at most 512 rows run register-resident (qrb_panel_reg.cuh); taller panels keep
+// the shared-memory panel kernel.
+template <int MODE, typename TIn, typename TOut>
+static void launch_panel(const PanelArgs& pa, int64_t cb, cudaStream_t st) {
+  const int m = pa.n - pa.k0;
+  if (m <= 256) panel_reg_kernel<MODE, TIn, TOut, 1><<<(unsigned)cb, 256, 0, st>>>(pa);
+  else if (m <= 512) panel_reg_kernel<MODE, TIn, TOut, 2><<<(unsigned)cb, 256, 0, st>>>(pa);
+  else panel_kernel<MODE, TIn, TOut><<<(unsigned)cb, 256, panel_smem_bytes(m, pa.w), st>>>(pa);
+}
+
 // One CholeskyQR pass (reflection_no_reflectors.py:68-77): G = X^T X (+ mu I),
 // G = L_G D L_G^T by panels, then Q = X R^{-1} with R^{-1} = L_G^{-T} D^{-1/2}.
 //   pass 1: Q = X R^{-1};  pass 2: Q = X - X (I - R^{-1}) (only the small correction goes
@@ -251,8 +262,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
     pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = ws.W; pa.Wc = ws.Wc; pa.Bp = ws.Bp;
     pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
     QRB_LAUNCH(prof, F_CHOL_PANEL,
-               panel_kernel<PM_CHOL, float, float>
-               <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
+               (launch_panel<PM_CHOL, float, float>(pa, cb, st)));
     const int k1 = k0 + w;
     if (k1 < n)
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
@@ -296,8 +306,8 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
       pa.info = info;
       const size_t smem = panel_smem_bytes(n - k0, w);
       QRB_LAUNCH(prof, F_LU_PANEL,
-                 if (cur_in) panel_kernel<PM_PIVOT, T, float><<<(unsigned)cb, 256, smem, st>>>(pa);
-                 else panel_kernel<PM_PIVOT, float, float><<<(unsigned)cb, 256, smem, st>>>(pa));
+                 if (cur_in) launch_panel<PM_PIVOT, T, float>(pa, cb, st);
+                 else launch_panel<PM_PIVOT, float, float>(pa, cb, st));
       const int k1 = k0 + w;
       if (k1 < n) {
         TrailWArgs ta{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap};
@@ -333,8 +343,7 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
     pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
     pa.src = cur; pa.W = ws.W; pa.H = H; pa.tau = tau; pa.s = ws.s; pa.info = info;
     QRB_LAUNCH(prof, F_CHART_PANEL,
-               panel_kernel<PM_CHART, float, T>
-               <<<(unsigned)cb, 256, panel_smem_bytes(n - k0, w), st>>>(pa));
+               (launch_panel<PM_CHART, float, T>(pa, cb, st)));
     const int k1 = k0 + w;
     // The chart stays on float32 FMA tiles: tau_k = 2/(1+|y_k|^2) sits at 1 when d_k = 0,
     // and the 2^-21 products of 3xTF32 would push it below the tau >= 1 - 1e-6 gate.

@@ -26,6 +26,18 @@
 #include <float.h>
 #include <limits.h>
 
+// Phase timers for the test kit's profiling build only (off in the library).
+#ifdef QRB_PANEL_TIMERS
+__device__ long long g_panel_timers[8];
+#define QRB_PT(i)                                                         \
+  do {                                                                    \
+    __syncthreads();                                                      \
+    if (threadIdx.x == 0 && blockIdx.x == 0) g_panel_timers[i] = clock64(); \
+  } while (0)
+#else
+#define QRB_PT(i) do { } while (0)
+#endif
+
 namespace qrb {
 
 enum PanelMode : int { PM_PIVOT = 0, PM_CHOL = 1, PM_CHART = 2 };
@@ -79,6 +91,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
   const TIn* src = reinterpret_cast<const TIn*>(a.src) + mat_off(b, n);
   if (tid == 0) s_flags = 0;
 
+  QRB_PT(0);
   // ---- jitter (CHOL): mu = 1e-7 * mean(diag G)  (reflection_no_reflectors.py:74) ----
   if (MODE == PM_CHOL) {
     if (k0 == 0) {
@@ -116,6 +129,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
     __syncthreads();
   }
 
+  QRB_PT(1);
   // ---- column-by-column elimination inside the panel ----
   for (int c = 0; c < w; ++c) {
     if (MODE == PM_PIVOT) {
@@ -190,6 +204,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
 
   int* info = a.info + b;
 
+  QRB_PT(2);
   // ---- outputs ----
   if (MODE == PM_PIVOT) {
     int* orig = a.orig + b * n;
@@ -272,6 +287,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
     }
   }
 
+  QRB_PT(3);
   // ---- W = L21 * L11^{-1} for the trailing update (PIVOT, CHART; CHOL: of L_G^{-1}) ----
   if (k0 + w < n) {
     __syncthreads();
@@ -289,6 +305,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
       for (int c = lane; c < w; c += 32) W[(int64_t)(k0 + p) * a.ldw + c] = P[p * ldp + c];
   }
 
+  QRB_PT(4);
   __syncthreads();
   if (tid == 0 && s_flags) atomicOr(info, s_flags);
 }

@@ -1,0 +1,430 @@
+// qrb200 -- register-resident panel elimination (panels of at most 512 rows x 32 columns).
+//
+// Same contract and outputs as panel_kernel (qrb_panel.cuh) -- PM_PIVOT / PM_CHOL / PM_CHART --
+// but each thread keeps RPT whole panel rows in registers (row r = tid + 256 q), so a column
+// step costs a few shuffles and one or two barriers instead of shared-memory round trips:
+//   PM_PIVOT : the pivot is chosen among the live rows by (max |a|, then lowest CURRENT
+//              position), exactly getrf's choice.  Rows never move: a position <-> row map in
+//              shared memory replays getrf's row swaps, so ties and the final row order match
+//              the swapping algorithm.  The winner publishes its row; 2 barriers per column.
+//   PM_CHOL  : the pivot row's entries right of the diagonal are read from the symmetric
+//              column (U[c][j] = S[j][c]), so only the lower triangle of G is ever used and
+//              each row owner publishes one value; 1 barrier per column.
+//   PM_CHART : the owner of row c publishes it; 1 barrier per column.
+// W = L21 L11^{-1} and L11^{-1} are computed in registers (right-looking substitution).
+#pragma once
+#include "qrb_panel.cuh"
+
+namespace qrb {
+
+constexpr int PR_W = 32;  // maximum panel width handled here
+
+template <typename T>
+__device__ __forceinline__ void load_row32(const T* p, int w, bool vec, float (&x)[PR_W]) {
+  if (vec && w == PR_W) {
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+      for (int c = 0; c < PR_W; c += 4) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p + c));
+        x[c] = t.x; x[c + 1] = t.y; x[c + 2] = t.z; x[c + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < PR_W; c += 4) {
+        const uint2 t = __ldg(reinterpret_cast<const uint2*>(p + c));
+        const T* h = reinterpret_cast<const T*>(&t);
+        x[c] = to_f32(h[0]); x[c + 1] = to_f32(h[1]); x[c + 2] = to_f32(h[2]); x[c + 3] = to_f32(h[3]);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < PR_W; ++c) x[c] = (c < w) ? to_f32(p[c]) : 0.f;
+  }
+}
+
+__device__ __forceinline__ void store_row32(float* p, int w, bool vec, const float (&x)[PR_W]) {
+  if (vec && w == PR_W) {
+#pragma unroll
+    for (int c = 0; c < PR_W; c += 4)
+      *reinterpret_cast<float4*>(p + c) = make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < PR_W; ++c)
+      if (c < w) p[c] = x[c];
+  }
+}
+
+// x <- x * L11^{-1}  (L11 unit lower, L11[i][j] = Ls[i][j] for j < i), in registers.
+__device__ __forceinline__ void times_l11_inv(float (&x)[PR_W], const float (*Ls)[PR_W + 1],
+                                              int w) {
+#pragma unroll
+  for (int i = PR_W - 1; i >= 1; --i) {
+    if (i < w) {
+      const float wi = x[i];
+#pragma unroll
+      for (int j = 0; j < i; ++j) x[j] = fmaf(-wi, Ls[i][j], x[j]);
+    }
+  }
+}
+
+template <int MODE, typename TIn, typename TOut, int RPT>
+__global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(PanelArgs a) {
+  const int n = a.n, k0 = a.k0, w = a.w, m = n - k0;
+  const int64_t b = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+
+  __shared__ float prow[2][PR_W];
+  __shared__ float Ls[PR_W][PR_W + 1];   // multipliers of the pivot rows, by position
+  __shared__ float dpiv[PR_W];
+  __shared__ float red_v[2][8];
+  __shared__ int red_p[2][8], red_r[2][8];
+  __shared__ int rowpos[256 * RPT], posrow[256 * RPT];  // PIVOT: local row <-> position
+  __shared__ int oids[256 * RPT];
+  __shared__ float tpart[8][PR_W];
+  __shared__ int s_flags;
+  __shared__ float s_mu;
+
+  const TIn* src = reinterpret_cast<const TIn*>(a.src) + mat_off(b, n);
+  const bool vec = ((n & 3) == 0) && ((k0 & 3) == 0);
+  if (tid == 0) s_flags = 0;
+
+  // ---- jitter (CHOL, reflection_no_reflectors.py:74) ----
+  if (MODE == PM_CHOL) {
+    if (k0 == 0) {
+      float acc = 0.f;
+      for (int i = tid; i < n; i += 256) acc += to_f32(src[(int64_t)i * n + i]);
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
+      if (lane == 0) red_v[0][warp] = acc;
+      __syncthreads();
+      if (tid == 0) {
+        float t = 0.f;
+        for (int i = 0; i < 8; ++i) t += red_v[0][i];
+        s_mu = 1e-7f * (t / (float)n);
+        a.mu[b] = s_mu;
+      }
+    } else if (tid == 0) {
+      s_mu = a.mu[b];
+    }
+  }
+
+  QRB_PT(0);
+  // ---- load the rows ----
+  float x[RPT][PR_W];
+  bool live[RPT];
+#pragma unroll
+  for (int q = 0; q < RPT; ++q) {
+    const int r = tid + 256 * q;
+    live[q] = r < m;
+    if (r < m) load_row32(src + (int64_t)(k0 + r) * n + k0, w, vec, x[q]);
+    else {
+#pragma unroll
+      for (int c = 0; c < PR_W; ++c) x[q][c] = 0.f;
+    }
+    if (MODE == PM_PIVOT && r < 256 * RPT) { rowpos[r] = r; posrow[r] = r; }
+  }
+  __syncthreads();
+
+  QRB_PT(1);
+  // ---- column-by-column elimination ----
+#pragma unroll
+  for (int c = 0; c < PR_W; ++c) {
+    if (c >= w) break;
+    const int par = c & 1;
+    if (MODE == PM_PIVOT) {
+      // candidate key: |a| bits (monotone for non-negative floats; NaN counts as 0 and is
+      // flagged), then the lowest current position.  Warp reductions with redux.sync.
+      unsigned bv = 0u;
+      int bp = INT_MAX, br = -1;
+      bool bad = false;
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        if (live[q]) {
+          const int r = tid + 256 * q;
+          const float xv = x[q][c];
+          bad |= !isfinite(xv);
+          const unsigned v = isnan(xv) ? 0u : __float_as_uint(fabsf(xv));
+          const int p = rowpos[r];
+          if (v > bv || (v == bv && p < bp)) { bv = v; bp = p; br = r; }
+        }
+      }
+      if (bad) atomicOr(&s_flags, INFO_NONFINITE_INPUT);
+      const unsigned wv = __reduce_max_sync(0xffffffffu, bv);
+      const int wp = (int)__reduce_min_sync(0xffffffffu, (bv == wv) ? (unsigned)bp : 0xffffffffu);
+      const unsigned own = __ballot_sync(0xffffffffu, bv == wv && bp == wp);
+      const int wr = __shfl_sync(0xffffffffu, br, own ? (__ffs(own) - 1) : 0);
+      if (lane == 0) {
+        red_v[par][warp] = __uint_as_float(wv);
+        red_p[par][warp] = wp;
+        red_r[par][warp] = wr;
+      }
+      __syncthreads();
+      unsigned V = __float_as_uint(red_v[par][0]);
+      int Pp = red_p[par][0], Rw = red_r[par][0];
+#pragma unroll
+      for (int i = 1; i < 8; ++i) {
+        const unsigned vi = __float_as_uint(red_v[par][i]);
+        const int pi = red_p[par][i];
+        if (vi > V || (vi == V && pi < Pp)) { V = vi; Pp = pi; Rw = red_r[par][i]; }
+      }
+      // the winner publishes its row (U row c and its multipliers for columns < c)
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        if (tid + 256 * q == Rw) {
+#pragma unroll
+          for (int j = 0; j < PR_W; ++j) {
+            if (j < w) prow[par][j] = x[q][j];
+            if (j < c) Ls[c][j] = x[q][j];
+          }
+          live[q] = false;
+        }
+      }
+      if (tid == 0 && Pp != c) {  // replay getrf's swap of positions c and Pp
+        const int rc = posrow[c];
+        posrow[c] = Rw; posrow[Pp] = rc;
+        rowpos[Rw] = c; rowpos[rc] = Pp;
+      }
+      __syncthreads();
+      const float pv = prow[par][c];
+      const float scale = (pv != 0.f) ? 1.f / pv : 1.f;
+      if (tid == 0) {
+        dpiv[c] = pv;
+        if (pv == 0.f) atomicOr(&s_flags, INFO_LU_ZERO_PIVOT);
+      }
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        if (live[q]) {
+          const float l = x[q][c] * scale;
+          x[q][c] = l;
+#pragma unroll
+          for (int j = c + 1; j < PR_W; ++j)
+            if (j < w) x[q][j] = fmaf(-l, prow[par][j], x[q][j]);
+        }
+      }
+    } else {
+      // row c is the pivot row (no pivoting); rows c .. w-1 live in threads c .. w-1, q = 0
+      if (MODE == PM_CHOL) {
+        if (tid >= c && tid < w) prow[par][tid] = x[0][c];  // U[c][j] = S[j][c]
+      } else {
+        if (tid == c) {
+#pragma unroll
+          for (int j = 0; j < PR_W; ++j)
+            if (j < w) prow[par][j] = x[0][j];
+        }
+      }
+      if (tid == c) {
+#pragma unroll
+        for (int j = 0; j < PR_W; ++j)
+          if (j < c) Ls[c][j] = x[0][j];
+      }
+      __syncthreads();
+      // CHOL: the jitter enters with the diagonal entry when it becomes the pivot (adding it
+      // before or after the earlier updates of that entry differs only by rounding)
+      const float pv = prow[par][c] + ((MODE == PM_CHOL) ? s_mu : 0.f);
+      float piv = pv, sgn = 1.f, rpiv = 1.f;
+      if (MODE == PM_CHOL) {
+        if (!(pv > 0.f)) {
+          if (tid == 0) atomicOr(&s_flags, a.info_bit);
+          piv = 1.f;  // keep the arithmetic finite; the host reports the failure
+        }
+        rpiv = __frcp_rn(piv);
+        if (tid == 0) dpiv[c] = piv;
+      } else {
+        const float pp = 1.f - pv, pm = 1.f + pv;
+        sgn = (fabsf(pp) >= fabsf(pm)) ? 1.f : -1.f;
+        piv = (sgn > 0.f) ? pp : pm;
+        if (tid == 0) dpiv[c] = sgn;
+      }
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        const int r = tid + 256 * q;
+        if (r > c && r < m) {
+          // Cholesky scales by the reciprocal pivot (as potf2 does); the chart divides (:158)
+          const float l = (MODE == PM_CHOL) ? x[q][c] * rpiv : (-sgn * x[q][c]) / piv;
+          x[q][c] = l;
+#pragma unroll
+          for (int j = c + 1; j < PR_W; ++j)
+            if (j < w) x[q][j] = fmaf(-l, prow[par][j], x[q][j]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  QRB_PT(2);
+  // ---- outputs ----
+  int pos[RPT];
+#pragma unroll
+  for (int q = 0; q < RPT; ++q) {
+    const int r = tid + 256 * q;
+    pos[q] = (MODE == PM_PIVOT && r < m) ? rowpos[r] : r;
+  }
+  float* Wb = a.W + (int64_t)b * n * a.ldw;
+
+  if (MODE == PM_PIVOT) {
+    int* orig = a.orig + b * n;
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+      const int r = tid + 256 * q;
+      if (r < m) oids[r] = (k0 == 0) ? r : orig[k0 + r];
+    }
+    __syncthreads();
+    for (int p = tid; p < m; p += 256) {
+      const int r = posrow[p];
+      orig[k0 + p] = oids[r];
+      a.srcmap[b * n + k0 + p] = k0 + r;
+    }
+    float* L = a.L + mat_off(b, n);
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+      const int r = tid + 256 * q;
+      if (r >= m) continue;
+      float* Lrow = L + (int64_t)oids[r] * n;
+      const int p = pos[q];
+      if (p < w) {
+        float y[PR_W];
+#pragma unroll
+        for (int c = 0; c < PR_W; ++c) y[c] = (c < p) ? x[q][c] : (c == p ? 1.f : 0.f);
+        store_row32(Lrow + k0, w, vec, y);
+        // pivot rows are final: zero the rest of the L row
+        int j = k0 + w;
+        if (vec) for (; j + 4 <= n; j += 4) *reinterpret_cast<float4*>(Lrow + j) = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (; j < n; ++j) Lrow[j] = 0.f;
+      } else {
+        store_row32(Lrow + k0, w, vec, x[q]);
+      }
+    }
+  } else if (MODE == PM_CHOL) {
+    float* R = a.R + mat_off(b, n);
+    __shared__ float sqd[PR_W];
+    if (tid < w) sqd[tid] = __fsqrt_rn(dpiv[tid]);
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+      const int r = tid + 256 * q;
+      if (r >= m) continue;
+#pragma unroll
+      for (int c = 0; c < PR_W; ++c)
+        if (c < w && c <= r) R[(int64_t)(k0 + c) * n + k0 + r] = (c == r) ? sqd[c] : sqd[c] * x[q][c];
+      if (r >= w) {  // L21 D^{1/2} for the Cholesky trailing update
+        float* wc = a.Wc + ((int64_t)b * n + k0 + r) * a.ldw;
+        if (w == PR_W && (a.ldw & 3) == 0) {
+#pragma unroll
+          for (int c = 0; c < PR_W; c += 4)
+            *reinterpret_cast<float4*>(wc + c) =
+                make_float4(x[q][c] * sqd[c], x[q][c + 1] * sqd[c + 1], x[q][c + 2] * sqd[c + 2],
+                            x[q][c + 3] * sqd[c + 3]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < PR_W; ++c)
+            if (c < w) wc[c] = x[q][c] * sqd[c];
+        }
+      }
+    }
+    if (tid < w) a.D[b * n + k0 + tid] = dpiv[tid];
+    // rows [k0, k0+w) of L_G^{-1} before this panel (identity block included), columns < k1;
+    // one flat float4 copy over all threads (k0 % 4 == 0 here since n % 4 == 0 or k0 == 0)
+    {
+      const int cols = k0 + w;
+      if (vec && (cols & 3) == 0) {
+        const int per = cols >> 2;
+#pragma unroll 4
+        for (int idx = tid; idx < w * per; idx += 256) {
+          const int c = idx / per, j = (idx - c * per) * 4;
+          float4 v;
+          if (j + 3 < k0) {
+            v = *reinterpret_cast<const float4*>(R + (int64_t)(k0 + c) * n + j);
+          } else {
+            float t[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              t[u] = (j + u < k0) ? R[(int64_t)(k0 + c) * n + j + u] : ((j + u == k0 + c) ? 1.f : 0.f);
+            v = make_float4(t[0], t[1], t[2], t[3]);
+          }
+          *reinterpret_cast<float4*>(a.Bp + ((int64_t)b * a.ldw + c) * n + j) = v;
+        }
+      } else {
+        for (int idx = tid; idx < w * cols; idx += 256) {
+          const int c = idx / cols, j = idx - c * cols;
+          a.Bp[((int64_t)b * a.ldw + c) * n + j] =
+              (j < k0) ? R[(int64_t)(k0 + c) * n + j] : ((j == k0 + c) ? 1.f : 0.f);
+        }
+      }
+    }
+    // L11^{-1} (unit lower) into rows [k0, k0+w) of the W buffer: row i of L11^{-1} is
+    // e_i^T L11^{-1}, computed by thread i in the registers of its (pivot) row, which is done
+    if (tid < w) {
+#pragma unroll
+      for (int c = 0; c < PR_W; ++c) x[0][c] = (c == tid) ? 1.f : 0.f;
+      times_l11_inv(x[0], Ls, w);
+      store_row32(Wb + (int64_t)(k0 + tid) * a.ldw, w, (a.ldw & 3) == 0, x[0]);
+    }
+  } else {  // PM_CHART
+    TOut* H = reinterpret_cast<TOut*>(a.H) + mat_off(b, n);
+    float part[PR_W];
+#pragma unroll
+    for (int c = 0; c < PR_W; ++c) part[c] = 0.f;
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+      const int r = tid + 256 * q;
+      if (r >= m) continue;
+      TOut* Hrow = H + (int64_t)(k0 + r) * n + k0;
+      if (r >= PR_W && w == PR_W && vec) {  // whole row below the panel: vector stores
+#pragma unroll
+        for (int c = 0; c < PR_W; c += 4) {
+          if constexpr (sizeof(TOut) == 4) {
+            *reinterpret_cast<float4*>(Hrow + c) =
+                make_float4(x[q][c], x[q][c + 1], x[q][c + 2], x[q][c + 3]);
+          } else {
+            TOut t[4] = {from_f32<TOut>(x[q][c]), from_f32<TOut>(x[q][c + 1]),
+                         from_f32<TOut>(x[q][c + 2]), from_f32<TOut>(x[q][c + 3])};
+            *reinterpret_cast<uint2*>(Hrow + c) = *reinterpret_cast<const uint2*>(t);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < PR_W; ++c) part[c] = fmaf(x[q][c], x[q][c], part[c]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < PR_W; ++c) {
+          if (c < w && c < r) {
+            Hrow[c] = from_f32<TOut>(x[q][c]);
+            part[c] = fmaf(x[q][c], x[q][c], part[c]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < PR_W; ++c) {
+      float v = part[c];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+      if (lane == 0) tpart[warp][c] = v;
+    }
+    __syncthreads();
+    if (tid < w) {
+      float acc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc += tpart[i][tid];
+      reinterpret_cast<TOut*>(a.tau)[b * n + k0 + tid] = from_f32<TOut>(2.f / (acc + 1.f));
+      a.s[b * n + k0 + tid] = dpiv[tid];
+    }
+  }
+
+  QRB_PT(3);
+  // ---- W = L21 L11^{-1} for the rows below the panel (positions >= w) ----
+  if (k0 + w < n) {
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+      const int r = tid + 256 * q;
+      if (r < m && pos[q] >= w) {
+        times_l11_inv(x[q], Ls, w);
+        store_row32(Wb + (int64_t)(k0 + pos[q]) * a.ldw, w, (a.ldw & 3) == 0, x[q]);
+      }
+    }
+  }
+
+  QRB_PT(4);
+  __syncthreads();
+  if (tid == 0 && s_flags) atomicOr(a.info + b, s_flags);
+}
+
+}  // namespace qrb

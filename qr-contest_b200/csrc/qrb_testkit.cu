@@ -91,3 +91,52 @@ int qrbt_qapply(const float* X, const float* RL, const float* D, float* Q, int* 
 }
 
 }  // extern "C"
+
+// ---- panel phase timing (built with QRB_PANEL_TIMERS) ----
+#include "qrb_panel_reg.cuh"
+
+template <int MODE>
+static int panel_timing_impl(const float* src, int64_t batch, int n, int k0, int w, int reg,
+                             long long* cycles_out, float* ms_out) {
+  const size_t nn = (size_t)n * n;
+  float *L, *R, *W, *Wc, *Bp, *D, *mu, *s, *tau, *H;
+  int *orig, *srcmap, *info;
+  cudaMalloc(&L, batch * nn * 4); cudaMalloc(&R, batch * nn * 4); cudaMalloc(&H, batch * nn * 4);
+  cudaMalloc(&W, batch * n * 32 * 4); cudaMalloc(&Wc, batch * n * 32 * 4);
+  cudaMalloc(&Bp, batch * n * 32 * 4); cudaMalloc(&D, batch * n * 4); cudaMalloc(&mu, batch * 4);
+  cudaMalloc(&s, batch * n * 4); cudaMalloc(&tau, batch * n * 4);
+  cudaMalloc(&orig, batch * n * 4); cudaMalloc(&srcmap, batch * n * 4); cudaMalloc(&info, batch * 4);
+  cudaMemset(R, 0, batch * nn * 4); cudaMemset(info, 0, batch * 4); cudaMemset(mu, 0, batch * 4);
+  PanelArgs pa{};
+  pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = 32; pa.src = src; pa.orig = orig; pa.srcmap = srcmap;
+  pa.W = W; pa.L = L; pa.R = R; pa.D = D; pa.Wc = Wc; pa.Bp = Bp; pa.mu = mu; pa.H = H;
+  pa.tau = tau; pa.s = s; pa.info = info; pa.info_bit = 2;
+  const size_t smem = panel_smem_bytes(n - k0, w);
+  cudaFuncSetAttribute(panel_kernel<MODE, float, float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       225 * 1024);
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0); cudaEventCreate(&e1);
+  auto launch = [&]() {
+    if (reg && n - k0 <= 256) panel_reg_kernel<MODE, float, float, 1><<<(unsigned)batch, 256>>>(pa);
+    else if (reg) panel_reg_kernel<MODE, float, float, 2><<<(unsigned)batch, 256>>>(pa);
+    else panel_kernel<MODE, float, float><<<(unsigned)batch, 256, smem>>>(pa);
+  };
+  launch();  // warm
+  cudaEventRecord(e0);
+  launch();
+  cudaEventRecord(e1);
+  cudaEventSynchronize(e1);
+  cudaEventElapsedTime(ms_out, e0, e1);
+  cudaMemcpyFromSymbol(cycles_out, g_panel_timers, 8 * sizeof(long long));
+  int rc = (int)cudaGetLastError();
+  cudaFree(L); cudaFree(R); cudaFree(H); cudaFree(W); cudaFree(Wc); cudaFree(Bp); cudaFree(D);
+  cudaFree(mu); cudaFree(s); cudaFree(tau); cudaFree(orig); cudaFree(srcmap); cudaFree(info);
+  return rc;
+}
+
+extern "C" int qrbt_panel_timing(int mode, const float* src, int64_t batch, int n, int k0, int w,
+                                 int reg, long long* cycles_out, float* ms_out) {
+  if (mode == 0) return panel_timing_impl<PM_PIVOT>(src, batch, n, k0, w, reg, cycles_out, ms_out);
+  if (mode == 1) return panel_timing_impl<PM_CHOL>(src, batch, n, k0, w, reg, cycles_out, ms_out);
+  return panel_timing_impl<PM_CHART>(src, batch, n, k0, w, reg, cycles_out, ms_out);
+}

@@ -51,9 +51,10 @@ def _compile(src: Path, out: Path, verbose: bool, extra) -> None:
 
 
 def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
-    for src, out in ((CSRC / "qrb_api.cu", LIB), (CSRC / "qrb_testkit.cu", TESTKIT)):
+    for src, out, defs in ((CSRC / "qrb_api.cu", LIB, []),
+                           (CSRC / "qrb_testkit.cu", TESTKIT, ["-DQRB_PANEL_TIMERS"])):
         if force or not up_to_date(out):
-            _compile(src, out, verbose, extra)
+            _compile(src, out, verbose, [*extra, *defs])
     return LIB
 
 
