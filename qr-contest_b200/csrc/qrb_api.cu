@@ -17,6 +17,7 @@
 #include "qrb_panel_reg.cuh"
 #include "qrb_tc_ops.cuh"
 #include "qrb_rankw.cuh"
+#include "qrb_tc_rankw.cuh"
 
 #include <atomic>
 #include <mutex>
@@ -142,6 +143,9 @@ static Ws carve(void* base, int64_t cb, int n, int nbmax) {
 static inline dim3 tiles_grid(int M, int N, int64_t cb) {
   return dim3((N + GT - 1) / GT, (M + GT - 1) / GT, (unsigned)cb);
 }
+static inline dim3 rwt_grid(int M, int N, int64_t cb) {
+  return dim3((N + 127) / 128, (M + 127) / 128, (unsigned)cb);
+}
 static inline dim3 rw_grid(int M, int N, int64_t cb) {
   return dim3((N + RW_N - 1) / RW_N, (M + RW_M - 1) / RW_M, (unsigned)cb);
 }
@@ -158,6 +162,12 @@ static inline bool use_tc(int n) {
 // the LU trailing update through the tcgen05 tiles instead (comparison runs).
 static inline bool use_rankw(int n) {
   return (n & 3) == 0 && g_gemm_path.load(std::memory_order_relaxed) != 2;
+}
+
+template <class Pb>
+static cudaError_t rwt_attr() {
+  return cudaFuncSetAttribute(tc::tc_rankw_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              tc::RWT_SMEM);
 }
 
 template <class Pb>
@@ -207,7 +217,12 @@ static cudaError_t set_common_attrs() {
   if ((e = tc_attr<tc::ClosureTC<__half>>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::TrailWTC<float>>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::TrailWTC<__nv_bfloat16>>()) != cudaSuccess) return e;
-  return tc_attr<tc::TrailWTC<__half>>();
+  if ((e = tc_attr<tc::TrailWTC<__half>>()) != cudaSuccess) return e;
+  if ((e = rwt_attr<RWSyrk>()) != cudaSuccess) return e;
+  if ((e = rwt_attr<RWLinv>()) != cudaSuccess) return e;
+  if ((e = rwt_attr<RWTrail<float>>()) != cudaSuccess) return e;
+  if ((e = rwt_attr<RWTrail<__nv_bfloat16>>()) != cudaSuccess) return e;
+  return rwt_attr<RWTrail<__half>>();
 }
 
 static cudaError_t ensure_attrs() {
@@ -266,13 +281,19 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
     const int k1 = k0 + w;
     if (k1 < n)
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 if (rw) rankw_kernel<RWSyrk><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
-                     RWSyrkArgs{n, k0, k1, nb, ws.T0, ws.R, ws.Wc});
+                 if (tcp && rw) tc::tc_rankw_kernel<RWSyrk>
+                     <<<rwt_grid(n - k1, n - k1, cb), 256, tc::RWT_SMEM, st>>>(
+                         RWSyrkArgs{n, k0, k1, nb, ws.T0, ws.R, ws.Wc, info});
+                 else if (rw) rankw_kernel<RWSyrk><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                     RWSyrkArgs{n, k0, k1, nb, ws.T0, ws.R, ws.Wc, info});
                  else simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
                      TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
     QRB_LAUNCH(prof, F_CHOL_TRAIL,
-               if (rw) rankw_kernel<RWLinv><<<rw_grid(n - k0, k1, cb), 256, 0, st>>>(
-                   RWLinvArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp});
+               if (tcp && rw) tc::tc_rankw_kernel<RWLinv>
+                   <<<rwt_grid(n - k0, k1, cb), 256, tc::RWT_SMEM, st>>>(
+                       RWLinvArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp, info});
+               else if (rw) rankw_kernel<RWLinv><<<rw_grid(n - k0, k1, cb), 256, 0, st>>>(
+                   RWLinvArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp, info});
                else simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k0, k1, cb), 256, 0, st>>>(
                    LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp}));
   }
@@ -314,10 +335,14 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
         const dim3 g = tiles_grid(n - k1, n - k1, cb);
         const tc::TrailWTCArgs tca{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap, info};
         const dim3 gt = tc_grid(n - k1, n - k1, cb);
-        const RWTrailArgs rwa{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap};
+        const RWTrailArgs rwa{n, k0, k1, nb, cur, Tb[ti], ws.W, ws.srcmap, info};
         const dim3 gr = rw_grid(n - k1, n - k1, cb);
         QRB_LAUNCH(prof, F_LU_TRAIL,
-                   if (rw && cur_in) rankw_kernel<RWTrail<T>><<<gr, 256, 0, st>>>(rwa);
+                   if (tcp && rw && cur_in) tc::tc_rankw_kernel<RWTrail<T>>
+                       <<<rwt_grid(n - k1, n - k1, cb), 256, tc::RWT_SMEM, st>>>(rwa);
+                   else if (tcp && rw) tc::tc_rankw_kernel<RWTrail<float>>
+                       <<<rwt_grid(n - k1, n - k1, cb), 256, tc::RWT_SMEM, st>>>(rwa);
+                   else if (rw && cur_in) rankw_kernel<RWTrail<T>><<<gr, 256, 0, st>>>(rwa);
                    else if (rw) rankw_kernel<RWTrail<float>><<<gr, 256, 0, st>>>(rwa);
                    else if (tcp && cur_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, 128>
                        <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
@@ -350,7 +375,7 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
     if (k1 < n)
       QRB_LAUNCH(prof, F_CHART_TRAIL,
                  if (rw) rankw_kernel<RWTrail<float>><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
-                     RWTrailArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr});
+                     RWTrailArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr, info});
                  else simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
                      TrailWArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr}));
   }

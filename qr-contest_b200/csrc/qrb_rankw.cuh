@@ -12,7 +12,8 @@
 // Policy Pb supplies: Args; dims(a, M, N, K); live(a, m0, n0);
 //   a_ptr(a, b, m)  -> const float*  row m of A (K contiguous floats, 16-byte aligned)
 //   b_ptr(a, b, k)  -> const TB*     row k of B (B(k, j) = p[j], j < N, 16-byte aligned)
-//   epi4(a, b, m, j, acc[4])         columns j .. j+3 of row m (j % 4 == 0, j + 3 < N)
+//   c_load4(a, b, m, j) -> float4    C_in of columns j .. j+3 of row m (j % 4 == 0)
+//   store4(a, b, m, j, C_in - acc)   the result of the same 4 columns
 // Requires n % 4 == 0 (callers fall back to the scalar tiles otherwise).
 #pragma once
 #include "qrb_common.cuh"
@@ -93,7 +94,12 @@ __global__ void __launch_bounds__(256) rankw_kernel(typename Pb::Args a) {
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int j = n0 + tn * 8 + 4 * h;
-      if (j < N) Pb::epi4(a, b, m, j, &acc[i][4 * h]);
+      if (j < N) {
+        float4 x = Pb::c_load4(a, b, m, j);
+        x.x -= acc[i][4 * h]; x.y -= acc[i][4 * h + 1];
+        x.z -= acc[i][4 * h + 2]; x.w -= acc[i][4 * h + 3];
+        Pb::store4(a, b, m, j, x);
+      }
     }
   }
 }
@@ -105,10 +111,12 @@ struct RWTrailArgs {
   float* Cnew;
   const float* W;
   const int* srcmap;  // nullptr -> identity
+  int* info;
 };
 template <typename T>
 struct RWTrail {
   using Args = RWTrailArgs;
+  __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
     M = N = a.n - a.k1;
     K = a.k1 - a.k0;
@@ -124,13 +132,14 @@ struct RWTrail {
     return reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
            (int64_t)srow(a, b, a.k0 + k) * a.n + a.k1;
   }
-  __device__ static void epi4(const Args& a, int64_t b, int m, int j, const float* v) {
+  __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
     const T* c = reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
                  (int64_t)srow(a, b, a.k1 + m) * a.n + a.k1 + j;
-    float4 x = (reinterpret_cast<const void*>(a.Cold) == reinterpret_cast<const void*>(a.Cnew))
-                   ? ld4rw(reinterpret_cast<const float*>(c))
-                   : ld4v(c);
-    x.x -= v[0]; x.y -= v[1]; x.z -= v[2]; x.w -= v[3];
+    // the chart updates in place: plain loads for a buffer this kernel also writes
+    return (a.Cold == static_cast<const void*>(a.Cnew)) ? ld4rw(reinterpret_cast<const float*>(c))
+                                                        : ld4v(c);
+  }
+  __device__ static void store4(const Args& a, int64_t b, int m, int j, float4 x) {
     st4(a.Cnew + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j, x);
   }
 };
@@ -141,9 +150,11 @@ struct RWSyrkArgs {
   float* G;
   const float* R;   // rows [k0, k1): R12 = D^{1/2} L21^T
   const float* Wc;  // rows [k1, n): L21 D^{1/2}
+  int* info;
 };
 struct RWSyrk {
   using Args = RWSyrkArgs;
+  __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
     M = N = a.n - a.k1;
     K = a.k1 - a.k0;
@@ -155,12 +166,13 @@ struct RWSyrk {
   __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
     return a.R + mat_off(b, a.n) + (int64_t)(a.k0 + k) * a.n + a.k1;
   }
-  __device__ static void epi4(const Args& a, int64_t b, int m, int j, const float* v) {
-    if (j > m + 3) return;  // strictly upper 4-block: never read
-    float* g = a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j;
-    float4 x = ld4rw(g);
-    x.x -= v[0]; x.y -= v[1]; x.z -= v[2]; x.w -= v[3];
-    st4(g, x);
+  __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
+    if (j > m + 3) return make_float4(0.f, 0.f, 0.f, 0.f);  // strictly upper: never read
+    return ld4rw(a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j);
+  }
+  __device__ static void store4(const Args& a, int64_t b, int m, int j, float4 x) {
+    if (j > m + 3) return;
+    st4(a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j, x);
   }
 };
 
@@ -175,9 +187,11 @@ struct RWLinvArgs {
   float* RL;
   const float* Wl;  // rows [k0, n): L11^{-1} then W
   const float* Bp;  // [ldw][n] per matrix: raw panel rows, columns [0, k1)
+  int* info;
 };
 struct RWLinv {
   using Args = RWLinvArgs;
+  __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
     M = a.n - a.k0;
     N = a.k1;
@@ -190,23 +204,22 @@ struct RWLinv {
   __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
     return a.Bp + ((int64_t)b * a.ldw + k) * a.n;
   }
-  __device__ static void epi4(const Args& a, int64_t b, int m, int j, const float* v) {
+  // C_in: L_G^{-1}[r][j] for j < k0 on rows below the panel; 0 on the panel's own columns
+  // (identity block) and on the panel rows, which are replaced outright (k0 % 4 == 0).
+  __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
+    const int r = a.k0 + m;
+    if (r < a.k1 || j >= a.k0) return make_float4(0.f, 0.f, 0.f, 0.f);
+    return ld4rw(a.RL + mat_off(b, a.n) + (int64_t)r * a.n + j);
+  }
+  __device__ static void store4(const Args& a, int64_t b, int m, int j, float4 x) {
     const int r = a.k0 + m;
     float* p = a.RL + mat_off(b, a.n) + (int64_t)r * a.n + j;
-    if (r < a.k1) {
+    if (r < a.k1) {  // panel row: result is +L11^{-1} B (the kernel computed 0 - acc)
+      const float t[4] = {-x.x, -x.y, -x.z, -x.w};
 #pragma unroll
-      for (int t = 0; t < 4; ++t)
-        if (j + t < r) p[t] = v[t];
+      for (int q = 0; q < 4; ++q)
+        if (j + q < r) p[q] = t[q];
     } else {
-      float4 x = (j + 3 < a.k0) ? ld4rw(p) : make_float4(0.f, 0.f, 0.f, 0.f);
-      if (j < a.k0 && j + 3 >= a.k0) {  // straddles k0 (k0 % 4 == 0 makes this impossible)
-        const float t[4] = {p[0], p[1], p[2], p[3]};
-        x.x = (j + 0 < a.k0) ? t[0] : 0.f;
-        x.y = (j + 1 < a.k0) ? t[1] : 0.f;
-        x.z = (j + 2 < a.k0) ? t[2] : 0.f;
-        x.w = (j + 3 < a.k0) ? t[3] : 0.f;
-      }
-      x.x -= v[0]; x.y -= v[1]; x.z -= v[2]; x.w -= v[3];
       st4(p, x);
     }
   }

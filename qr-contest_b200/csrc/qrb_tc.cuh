@@ -298,3 +298,4 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_gemm_kernel(typename Pb::Args 
 
 }  // namespace tc
 }  // namespace qrb
+

@@ -5,6 +5,7 @@
 #include "qrb_common.cuh"
 #include "qrb_gemm_simt.cuh"
 #include "qrb_tc_ops.cuh"
+#include "qrb_tc_rankw.cuh"
 
 using namespace qrb;
 
@@ -35,7 +36,16 @@ int qrbt_gram(const float* X, float* G, int* info, int64_t batch, int n, int use
 int qrbt_trailw(const float* Cold, float* Cnew, const float* W, const int* srcmap, int* info,
                 int64_t batch, int n, int k0, int k1, int ldw, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
-  if (use_tc) {
+  // use_tc: 0 scalar tiles, 1 tcgen05 GEMM tile, 2 tcgen05 rank-w tile, 3 streaming rank-w tile
+  const RWTrailArgs rwa{n, k0, k1, ldw, Cold, Cnew, W, srcmap, info};
+  if (use_tc == 2) {
+    cudaFuncSetAttribute(tc::tc_rankw_kernel<RWTrail<float>>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, tc::RWT_SMEM);
+    tc::tc_rankw_kernel<RWTrail<float>><<<g128(n - k1, n - k1, batch), 256, tc::RWT_SMEM, s>>>(rwa);
+  } else if (use_tc == 3) {
+    rankw_kernel<RWTrail<float>><<<dim3((n - k1 + 127) / 128, (n - k1 + 63) / 64, (unsigned)batch),
+                                   256, 0, s>>>(rwa);
+  } else if (use_tc) {
     if (int e = prep<tc::TrailWTC<float>>()) return e;
     tc::tc_gemm_kernel<tc::TrailWTC<float>, 128><<<g128(n - k1, n - k1, batch), tc::NTHREADS,
                                                    kSm, s>>>(

@@ -52,7 +52,7 @@ def test_gram(tc, n):
     assert int(info.sum()) == 0
 
 
-@pytest.mark.parametrize("tc", [0, 1])
+@pytest.mark.parametrize("tc", [0, 1, 2, 3])
 @pytest.mark.parametrize("gather", [False, True])
 @pytest.mark.parametrize("n,k0,k1", [(256, 32, 64), (512, 0, 32), (192, 160, 176)])
 def test_trailw(tc, gather, n, k0, k1):
