@@ -18,8 +18,11 @@
 #include "qrb_tc_ops.cuh"
 #include "qrb_rankw.cuh"
 #include "qrb_tc_rankw.cuh"
+#include "qrb_tcx.cuh"
+#include "qrb_tmap.cuh"
 
 #include <atomic>
+#include <type_traits>
 #include <mutex>
 #include <utility>
 #include <vector>
@@ -164,6 +167,22 @@ static inline bool use_rankw(int n) {
   return (n & 3) == 0 && g_gemm_path.load(std::memory_order_relaxed) != 2;
 }
 
+// Output tile of the tcgen05 GEMMs: 128 x kTcBN (64 was measured slower: twice the loader work per flop).
+constexpr int kTcBN = 128;
+
+template <class Pb>
+static cudaError_t tcx_attr() {
+  return cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              tcx::SMEM_BYTES);
+}
+
+// TMA maps for a tcx launch: operands stored k-major use 128-row boxes, m-major 32-row boxes.
+static bool tcx_maps(tcx::Maps& mp, const void* a, bool a_kmajor, const void* b, bool b_kmajor,
+                     int n, int64_t cb) {
+  return encode_batched(&mp.a, a, n, cb, a_kmajor ? 128 : 32) &&
+         encode_batched(&mp.b, b, n, cb, b_kmajor ? 128 : 32);
+}
+
 template <class Pb>
 static cudaError_t rwt_attr() {
   return cudaFuncSetAttribute(tc::tc_rankw_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -172,14 +191,14 @@ static cudaError_t rwt_attr() {
 
 template <class Pb>
 static cudaError_t tc_attr() {
-  return cudaFuncSetAttribute(tc::tc_gemm_kernel<Pb, 128>,
+  return cudaFuncSetAttribute(tc::tc_gemm_kernel<Pb, kTcBN>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              tc::SmemLayout<128>::TOTAL);
+                              tc::SmemLayout<kTcBN>::TOTAL);
 }
 static inline dim3 tc_grid(int M, int N, int64_t cb) {
-  return dim3((N + 127) / 128, (M + tc::BM - 1) / tc::BM, (unsigned)cb);
+  return dim3((N + kTcBN - 1) / kTcBN, (M + tc::BM - 1) / tc::BM, (unsigned)cb);
 }
-constexpr size_t kTcSmem = tc::SmemLayout<128>::TOTAL;
+constexpr size_t kTcSmem = tc::SmemLayout<kTcBN>::TOTAL;
 
 // Raise the dynamic shared-memory limit of every big-smem kernel once per device.
 template <typename TIn>
@@ -222,7 +241,10 @@ static cudaError_t set_common_attrs() {
   if ((e = rwt_attr<RWLinv>()) != cudaSuccess) return e;
   if ((e = rwt_attr<RWTrail<float>>()) != cudaSuccess) return e;
   if ((e = rwt_attr<RWTrail<__nv_bfloat16>>()) != cudaSuccess) return e;
-  return rwt_attr<RWTrail<__half>>();
+  if ((e = rwt_attr<RWTrail<__half>>()) != cudaSuccess) return e;
+  if ((e = tcx_attr<tcx::GramX>()) != cudaSuccess) return e;
+  if ((e = tcx_attr<tcx::QApplyX>()) != cudaSuccess) return e;
+  return tcx_attr<tcx::ClosureX>();
 }
 
 static cudaError_t ensure_attrs() {
@@ -261,8 +283,13 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   const bool tcp = use_tc(n);
   const bool rw = use_rankw(n);
   const bool pass2 = (info_bit == INFO_CHOL2_NOT_PD);
+  tcx::Maps gm;
+  const bool gx = tcp && tcx_maps(gm, X, false, X, false, n, cb);
   QRB_LAUNCH(prof, F_GRAM,
-             if (tcp) tc::tc_gemm_kernel<tc::GramTC, 128><<<tc_grid(n, n, cb), tc::NTHREADS,
+             if (gx) tcx::tcx_gemm_kernel<tcx::GramX><<<tc_grid(n, n, cb), tc::NTHREADS,
+                                                        tcx::SMEM_BYTES, st>>>(
+                 gm, tc::GramTCArgs{n, X, ws.T0, info});
+             else if (tcp) tc::tc_gemm_kernel<tc::GramTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                kTcSmem, st>>>(
                  tc::GramTCArgs{n, X, ws.T0, info});
              else simt_gemm_kernel<Gram><<<tiles_grid(n, n, cb), 256, 0, st>>>(
@@ -298,8 +325,12 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
                    LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp}));
   }
   const QApplyArgs qa{n, pass2 ? 1 : 0, X, ws.R, ws.D, Q, info};
+  tcx::Maps qm;
+  const bool qx = tcp && tcx_maps(qm, X, true, ws.R, true, n, cb);
   QRB_LAUNCH(prof, F_QAPPLY,
-             if (tcp) tc::tc_gemm_kernel<tc::QApplyTC, 128><<<tc_grid(n, n, cb), tc::NTHREADS,
+             if (qx) tcx::tcx_gemm_kernel<tcx::QApplyX><<<tc_grid(n, n, cb), tc::NTHREADS,
+                                                          tcx::SMEM_BYTES, st>>>(qm, qa);
+             else if (tcp) tc::tc_gemm_kernel<tc::QApplyTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                 kTcSmem, st>>>(qa);
              else simt_gemm_kernel<QApply><<<tiles_grid(n, n, cb), 256, 0, st>>>(qa));
 }
@@ -344,9 +375,9 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
                        <<<rwt_grid(n - k1, n - k1, cb), 256, tc::RWT_SMEM, st>>>(rwa);
                    else if (rw && cur_in) rankw_kernel<RWTrail<T>><<<gr, 256, 0, st>>>(rwa);
                    else if (rw) rankw_kernel<RWTrail<float>><<<gr, 256, 0, st>>>(rwa);
-                   else if (tcp && cur_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, 128>
+                   else if (tcp && cur_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, kTcBN>
                        <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
-                   else if (tcp) tc::tc_gemm_kernel<tc::TrailWTC<float>, 128>
+                   else if (tcp) tc::tc_gemm_kernel<tc::TrailWTC<float>, kTcBN>
                        <<<gt, tc::NTHREADS, kTcSmem, st>>>(tca);
                    else if (cur_in) simt_gemm_kernel<TrailW<T>><<<g, 256, 0, st>>>(ta);
                    else simt_gemm_kernel<TrailW<float>><<<g, 256, 0, st>>>(ta));
@@ -380,8 +411,13 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
                      TrailWArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr}));
   }
   // ---- II: closure, H_upper = s * triu(Q^T A) ----
+  tcx::Maps cm;
+  const bool cx = tcp && std::is_same<T, float>::value && tcx_maps(cm, ws.L, false, A, false, n, cb);
   QRB_LAUNCH(prof, F_CLOSURE,
-             if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, 128>
+             if (cx) tcx::tcx_gemm_kernel<tcx::ClosureX><<<tc_grid(n, n, cb), tc::NTHREADS,
+                                                           tcx::SMEM_BYTES, st>>>(
+                 cm, tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
+             else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>
                  <<<tc_grid(n, n, cb), tc::NTHREADS, kTcSmem, st>>>(
                      tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
              else simt_gemm_kernel<Closure<T>><<<tiles_grid(n, n, cb), 256, 0, st>>>(

@@ -167,7 +167,7 @@ struct SmemLayout {
 };
 
 template <class Pb, int BN>
-__global__ void __launch_bounds__(NTHREADS, 1) tc_gemm_kernel(typename Pb::Args a) {
+__global__ void __launch_bounds__(NTHREADS, BN == 64 ? 2 : 1) tc_gemm_kernel(typename Pb::Args a) {
   using L = SmemLayout<BN>;
   extern __shared__ __align__(1024) char smraw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));

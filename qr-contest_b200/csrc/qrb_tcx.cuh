@@ -1,0 +1,222 @@
+// qrb200 -- TMA-fed 3xTF32 tcgen05 GEMM tile for the float32 n^3 stages (Grams, R^{-1} apply,
+// float32 closure).
+//
+// Same mathematics and policies as tc_gemm_kernel (qrb_tc.cuh / qrb_tc_ops.cuh), different
+// data movement: raw float32 tiles are brought into a shared-memory ring by
+// cp.async.bulk.tensor (3-deep ring, SWIZZLE_128B, completion counted on an mbarrier), so no
+// thread waits on global loads.  All 256 threads then split a raw tile into hi/lo tf32 planes
+// (two plane sets, so the split of stage t+1 overlaps the MMAs of stage t; K-major SW128,
+// the UMMA operand layout), transposing M-major tiles in registers; one elected thread issues
+// the 12 MMAs of the stage and commits to an mbarrier that frees the planes.  Raw tiles of an
+// operand stored M-major (A(m,k) = X[k][m]) arrive as four 32 x 32 boxes; K-major operands
+// (A(m,k) = X[m][k]) as one 128-row box.  Out-of-range boxes are zero-filled by the TMA unit.
+// No multicast: every CTA loads its own tiles (the library also runs on 2-8 GPUs).
+#pragma once
+#include <cuda.h>
+
+#include "qrb_tc_ops.cuh"
+
+namespace qrb {
+namespace tcx {
+
+using tc::BK;
+using tc::BM;
+using tc::NTHREADS;
+using tc::UK;
+
+constexpr int BN = 128;
+constexpr int RAW_STAGES = 3;
+constexpr int RAW_A = BM * BK * 4;   // 16 KB
+constexpr int RAW_B = BN * BK * 4;   // 16 KB
+constexpr int PLANE = 16384;         // one hi or lo plane of a 128 x 32 operand tile
+constexpr int PLANE_SETS = 2;      // split of stage t+1 overlaps the MMAs of stage t
+constexpr int SMEM_BYTES = RAW_STAGES * (RAW_A + RAW_B) + PLANE_SETS * 4 * PLANE + 1024 + 128;
+
+struct Maps {
+  CUtensorMap a;  // raw A source
+  CUtensorMap b;  // raw B source
+};
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc::smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(tc::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(tc::smem_u32(bar))
+      : "memory");
+}
+
+// Raw tile of an operand whose rows (tile rows = M or N index) are contiguous in k:
+// one box {32 k, 128 rows}.  Element (r, k) sits at sw128_off(r, k/4) + 4*(k%4).
+// Raw tile of an operand stored k-major (X[k][r]): four boxes {32 r, 32 k}, box i covering
+// rows 32i..32i+31; element (r, k) at i*4096 + sw128_off(k, (r%32)/4) + 4*(r%4).
+template <bool KMAJOR>
+__device__ __forceinline__ void issue_raw(char* dst, const CUtensorMap* map, int r0, int k0,
+                                          int z, uint64_t* bar) {
+  if (KMAJOR) {
+    tma_load_3d(dst, map, k0, r0, z, bar);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) tma_load_3d(dst + i * 4096, map, r0 + 32 * i, k0, z, bar);
+  }
+}
+
+// 4(row) x 4(k) micro-block (rows 4*rb.., k 4*kc..) out of a raw tile.
+template <bool KMAJOR>
+__device__ __forceinline__ void read_raw(const char* raw, int rb, int kc, float (&v)[4][4]) {
+  if (KMAJOR) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 t = *reinterpret_cast<const float4*>(raw + tc::sw128_off(4 * rb + i, kc));
+      v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
+    }
+  } else {
+    const char* blk = raw + (rb >> 3) * 4096;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const float4 t = *reinterpret_cast<const float4*>(blk + tc::sw128_off(4 * kc + kk, rb & 7));
+      v[0][kk] = t.x; v[1][kk] = t.y; v[2][kk] = t.z; v[3][kk] = t.w;
+    }
+  }
+}
+
+// Policy additions over the tc_ops policies: A_KMAJOR / B_KMAJOR (raw layout of the sources
+// described by the two tensor maps), fixA (elementwise transform of an A block, may be empty).
+template <class Pb>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tcx_gemm_kernel(const __grid_constant__ Maps maps, typename Pb::Args a) {
+  extern __shared__ __align__(1024) char smraw[];
+  char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  char* rawA = sm;                                  // [RAW_STAGES][RAW_A]
+  char* rawB = sm + RAW_STAGES * RAW_A;             // [RAW_STAGES][RAW_B]
+  char* pl0 = sm + RAW_STAGES * (RAW_A + RAW_B);    // [PLANE_SETS] x {a_hi, a_lo, b_hi, b_lo}
+  uint64_t* full = reinterpret_cast<uint64_t*>(pl0 + PLANE_SETS * 4 * PLANE);  // [RAW_STAGES]
+  uint64_t* mma_bar = full + RAW_STAGES;                                          // [PLANE_SETS]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_bar + PLANE_SETS);
+
+  const int64_t b = blockIdx.z;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  if (!Pb::live(m0, n0, BM, BN)) return;
+  int M, N, K;
+  Pb::dims(a, M, N, K);
+  if (m0 >= M || n0 >= N) return;
+  int kb, ke;
+  Pb::krange(a, m0, n0, kb, ke);
+  const int nk = (ke > kb) ? (ke - kb + BK - 1) / BK : 0;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  if (warp == 0) {
+    tc::tmem_alloc(tslot, BN);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < RAW_STAGES; ++s) tc::mbar_init(&full[s], 1);
+    for (int p = 0; p < PLANE_SETS; ++p) tc::mbar_init(&mma_bar[p], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  auto issue = [&](int t) {  // producer: raw tiles of k-step t into slot t % RAW_STAGES
+    const int s = t % RAW_STAGES, k0 = kb + t * BK;
+    mbar_expect_tx(&full[s], RAW_A + RAW_B);
+    issue_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, &maps.a, m0, k0, (int)b, &full[s]);
+    issue_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, &maps.b, n0, k0, (int)b, &full[s]);
+  };
+  if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
+    for (int t = 0; t < nk && t < RAW_STAGES; ++t) issue(t);
+  }
+
+  const int a_mb = tid >> 3, a_kc = tid & 7;   // A: 32 row blocks x 8 k chunks
+  const int b_jb = tid >> 3, b_kc = tid & 7;   // B: 32 column blocks x 8 k chunks
+  constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
+  bool ok = true;
+  for (int t = 0; t < nk; ++t) {
+    const int s = t % RAW_STAGES, k0 = kb + t * BK;
+    const int ps = t & 1;                 // plane set of this stage
+    char* pl = pl0 + ps * 4 * PLANE;
+    if (!tc::mbar_wait(&full[s], (t / RAW_STAGES) & 1)) ok = false;
+    // plane set ps was last read by the MMAs of stage t-2 (commit number t/2 - 1 on mma_bar[ps])
+    if (t >= 2 && !tc::mbar_wait(&mma_bar[ps], ((t >> 1) - 1) & 1)) ok = false;
+    float v[4][4];
+    read_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, a_mb, a_kc, v);
+    Pb::fixA(a, b, m0 + 4 * a_mb, k0 + 4 * a_kc, v);
+    tc::put4x4(pl, pl + PLANE, 4 * a_mb, a_kc, v);
+    read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, b_jb, b_kc, v);
+    Pb::fixB(a, b, n0 + 4 * b_jb, k0 + 4 * b_kc, v);
+    tc::put4x4(pl + 2 * PLANE, pl + 3 * PLANE, 4 * b_jb, b_kc, v);
+    tc::fence_async_smem();
+    tc::tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc::tc_fence_after();
+      if (t + RAW_STAGES < nk) issue(t + RAW_STAGES);  // slot s has been read by everyone
+      const uint32_t ah = tc::smem_u32(pl), al = tc::smem_u32(pl + PLANE);
+      const uint32_t bh = tc::smem_u32(pl + 2 * PLANE), bl = tc::smem_u32(pl + 3 * PLANE);
+#pragma unroll
+      for (int kk = 0; kk < BK / UK; ++kk) {
+        const uint32_t koff = kk * UK * 4;
+        const uint64_t dah = tc::sdesc_sw128(ah + koff), dal = tc::sdesc_sw128(al + koff);
+        const uint64_t dbh = tc::sdesc_sw128(bh + koff), dbl = tc::sdesc_sw128(bl + koff);
+        tc::mma_tf32(tmem, dal, dbh, IDESC, (t > 0 || kk > 0) ? 1u : 0u);
+        tc::mma_tf32(tmem, dah, dbl, IDESC, 1u);
+        tc::mma_tf32(tmem, dah, dbh, IDESC, 1u);
+      }
+      tc::mma_commit(&mma_bar[ps]);
+    }
+  }
+  // the last commit covers every MMA issued before it
+  if (nk >= 1) {
+    const int t = nk - 1;
+    if (!tc::mbar_wait(&mma_bar[t & 1], (t >> 1) & 1)) ok = false;
+  }
+  tc::tc_fence_after();
+
+  if (!ok) {
+    if (tid == 0) atomicOr(Pb::info(a, b), INFO_DEVICE_TIMEOUT);
+  } else {
+    const int lq = warp & 3;
+    const int m = m0 + 32 * lq + lane;
+    constexpr int CPW = BN / 2;
+    for (int c = 0; c < CPW; c += 32) {
+      const int col = (warp >> 2) * CPW + c;
+      float v[32];
+      if (nk > 0) tc::tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + col, v);
+      else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = 0.f;
+      }
+      if (m < M && n0 + col < N) Pb::store(a, b, m, n0 + col, v, M, N);
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, BN);
+}
+
+// ---- policies: the tc_ops ones plus the raw-layout flags ----
+struct GramX : tc::GramTC {
+  static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // X[k][m], X[k][j]
+  __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
+};
+struct QApplyX : tc::QApplyTC {
+  static constexpr bool A_KMAJOR = true, B_KMAJOR = true;    // X[m][k], RL[j][k]
+  __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
+};
+struct ClosureX : tc::ClosureTC<float> {
+  static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // Q[k][m], A[k][j]
+  __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
+};
+
+}  // namespace tcx
+}  // namespace qrb

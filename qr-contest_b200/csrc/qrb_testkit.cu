@@ -6,6 +6,8 @@
 #include "qrb_gemm_simt.cuh"
 #include "qrb_tc_ops.cuh"
 #include "qrb_tc_rankw.cuh"
+#include "qrb_tcx.cuh"
+#include "qrb_tmap.cuh"
 
 using namespace qrb;
 
@@ -19,11 +21,27 @@ static int prep() {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSm);
 }
 
+template <class Pb>
+static int tcx_launch(const void* a, bool ak, const void* b, bool bk, int n, int64_t batch,
+                      const typename Pb::Args& args, cudaStream_t s) {
+  tcx::Maps mp;
+  if (!encode_batched(&mp.a, a, n, batch, ak ? 128 : 32) ||
+      !encode_batched(&mp.b, b, n, batch, bk ? 128 : 32))
+    return 999;
+  cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       tcx::SMEM_BYTES);
+  tcx::tcx_gemm_kernel<Pb><<<g128(n, n, batch), 256, tcx::SMEM_BYTES, s>>>(mp, args);
+  return 0;
+}
+
 extern "C" {
 
 int qrbt_gram(const float* X, float* G, int* info, int64_t batch, int n, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
-  if (use_tc) {
+  if (use_tc == 2) {
+    if (int e = tcx_launch<tcx::GramX>(X, false, X, false, n, batch, tc::GramTCArgs{n, X, G, info}, s))
+      return e;
+  } else if (use_tc) {
     if (int e = prep<tc::GramTC>()) return e;
     tc::tc_gemm_kernel<tc::GramTC, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(
         tc::GramTCArgs{n, X, G, info});
@@ -74,7 +92,11 @@ int qrbt_syrk(float* G, const float* R, int* info, int64_t batch, int n, int k0,
 int qrbt_closure(const float* Q, const float* A, const float* sgn, float* H, int* info,
                  int64_t batch, int n, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
-  if (use_tc) {
+  if (use_tc == 2) {
+    if (int e = tcx_launch<tcx::ClosureX>(Q, false, A, false, n, batch,
+                                          tc::ClosureTCArgs{n, Q, A, sgn, H, info}, s))
+      return e;
+  } else if (use_tc) {
     if (int e = prep<tc::ClosureTC<float>>()) return e;
     tc::tc_gemm_kernel<tc::ClosureTC<float>, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(
         tc::ClosureTCArgs{n, Q, A, sgn, H, info});
@@ -91,7 +113,9 @@ int qrbt_qapply(const float* X, const float* RL, const float* D, float* Q, int* 
                 int64_t batch, int n, int pass2, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
   const QApplyArgs qa{n, pass2, X, RL, D, Q, info};
-  if (use_tc) {
+  if (use_tc == 2) {
+    if (int e = tcx_launch<tcx::QApplyX>(X, true, RL, true, n, batch, qa, s)) return e;
+  } else if (use_tc) {
     if (int e = prep<tc::QApplyTC>()) return e;
     tc::tc_gemm_kernel<tc::QApplyTC, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(qa);
   } else {
