@@ -137,6 +137,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int t = 0; t < nk && t < RAW_STAGES; ++t) issue(t);
   }
 
+  // Long reductions drain the TMEM accumulator into float32 registers every DRAIN stages:
+  // TMEM accumulation does not round to nearest on each add, and over K = 2048 the drift is
+  // large enough to make a Gram indefinite.  Short reductions (nk <= 2 * DRAIN) never drain.
+  constexpr int DRAIN = 8;
+  const bool drains = nk > 2 * DRAIN;
+  float racc[BN / 2];
+#pragma unroll
+  for (int i = 0; i < BN / 2; ++i) racc[i] = 0.f;
+  const int lq = warp & 3;
+
   const int a_mb = tid >> 3, a_kc = tid & 7;   // A: 32 row blocks x 8 k chunks
   const int b_jb = tid >> 3, b_kc = tid & 7;   // B: 32 column blocks x 8 k chunks
   constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
@@ -168,11 +178,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t koff = kk * UK * 4;
         const uint64_t dah = tc::sdesc_sw128(ah + koff), dal = tc::sdesc_sw128(al + koff);
         const uint64_t dbh = tc::sdesc_sw128(bh + koff), dbl = tc::sdesc_sw128(bl + koff);
-        tc::mma_tf32(tmem, dal, dbh, IDESC, (t > 0 || kk > 0) ? 1u : 0u);
+        const bool fresh = (drains ? (t % DRAIN == 0) : (t == 0)) && kk == 0;
+        tc::mma_tf32(tmem, dal, dbh, IDESC, fresh ? 0u : 1u);
         tc::mma_tf32(tmem, dah, dbl, IDESC, 1u);
         tc::mma_tf32(tmem, dah, dbh, IDESC, 1u);
       }
       tc::mma_commit(&mma_bar[ps]);
+    }
+    if (drains && (t + 1) % DRAIN == 0 && t + 1 < nk) {
+      if (!tc::mbar_wait(&mma_bar[ps], (t >> 1) & 1)) ok = false;
+      tc::tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < BN / 2; c += 32) {
+        float v[32];
+        tc::tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + (warp >> 2) * (BN / 2) + c, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) racc[c + i] += v[i];
+      }
+      tc::tc_fence_before();
+      __syncthreads();
     }
   }
   // the last commit covers every MMA issued before it
@@ -185,9 +209,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (!ok) {
     if (tid == 0) atomicOr(Pb::info(a, b), INFO_DEVICE_TIMEOUT);
   } else {
-    const int lq = warp & 3;
     const int m = m0 + 32 * lq + lane;
     constexpr int CPW = BN / 2;
+#pragma unroll
     for (int c = 0; c < CPW; c += 32) {
       const int col = (warp >> 2) * CPW + c;
       float v[32];
@@ -196,6 +220,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] += racc[c + i];
       if (m < M && n0 + col < N) Pb::store(a, b, m, n0 + col, v, M, N);
     }
   }

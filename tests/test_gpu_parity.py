@@ -174,3 +174,15 @@ def test_info_clean_on_valid_input():
 def test_cpu_tensor_rejected():
     with pytest.raises(ValueError):
         qrb().custom_kernel(torch.randn(2, 4, 4))
+
+
+@pytest.mark.parametrize("n", [1040, 2048])
+def test_large_n_gates(n):
+    # panels taller than 512 rows (shared-memory panel kernel), panel width 16 at n = 2048,
+    # long-K tensor-core Grams; the ill-conditioned large-n class of the benchmark configs
+    from qrb200 import generators as G
+    A = G.large_illcond(2, n, seed=4, device="cuda")
+    H, tau, info = qrb().geqrf(A)
+    torch.cuda.synchronize()
+    assert int(info.abs().sum()) == 0
+    assert_gates(A, H, tau, f"n={n}")

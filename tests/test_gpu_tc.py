@@ -152,3 +152,10 @@ def test_qapply(tc, pass2, n):
         ref = X64 @ Rinv
         bound = X64.abs() @ Rinv.abs()
     close(Q, ref, bound)
+
+
+@pytest.mark.parametrize("tc", [0, 2])
+def test_gram_long_k(tc):
+    # K = 2048: the TMA tile drains its TMEM accumulator into float32 registers every 256 k,
+    # which keeps the error inside the float32 bound (a single TMEM accumulation does not)
+    test_gram(tc, 2048)
