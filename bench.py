@@ -79,7 +79,7 @@ def family_flops(n: int) -> dict:
     """Algorithmic flops each kernel family performs on one matrix."""
     nb = nb_for(n)
     f = {k: 0.0 for k in ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "q_apply",
-                          "chart_panel", "chart_trail", "closure")}
+                          "chart_panel", "chart_trail", "closure", "small_fused")}
     for k0 in range(0, n, nb):
         w = min(nb, n - k0)
         m = n - k0

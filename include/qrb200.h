@@ -81,7 +81,7 @@ int qrb200_geqrf_batched_timed(const void* A, void* H, void* tau, int32_t* info,
 
 /* Number of kernel families reported by qrb200_geqrf_batched_timed, and their names
  * ("lu_panel", "lu_trail", "gram", "chol_panel", "chol_trail", "q_apply", "chart_panel",
- * "chart_trail", "closure").  No reference counterpart (the stage list of
+ * "chart_trail", "closure", "small_fused" -- the one-kernel path for n <= 128).  No reference counterpart (the stage list of
  * reflection_no_reflectors.py:55-196 as this library splits it into kernels). */
 int32_t qrb200_num_families(void);
 const char* qrb200_family_name(int32_t family);
@@ -95,6 +95,10 @@ long long qrb200_launch_count(void);
  *   SIMT float32 tiles otherwise), 1 = SIMT tiles only, 2 = tcgen05 tiles whenever n % 4 == 0.
  * Returns QRB200_ERR_INVALID_ARG for an unknown key or value. */
 #define QRB200_OPT_GEMM_PATH 1
+/*   QRB200_OPT_SMALL_N: largest n (0..128, default 64) factored by the fused kernel that keeps
+ *   the whole pipeline of one matrix in one CTA's shared memory (no workspace); larger n use
+ *   the staged kernels.  Changing it also changes qrb200_workspace_bytes. */
+#define QRB200_OPT_SMALL_N 2
 int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return

@@ -20,6 +20,7 @@
 #include "qrb_tc_rankw.cuh"
 #include "qrb_tcx.cuh"
 #include "qrb_tmap.cuh"
+#include "qrb_small.cuh"
 
 #include <atomic>
 #include <type_traits>
@@ -32,7 +33,7 @@ namespace qrb {
 // Kernel families, in the order of the per-family timings qrb200_geqrf_batched_timed returns.
 enum Family : int {
   F_LU_PANEL = 0, F_LU_TRAIL, F_GRAM, F_CHOL_PANEL, F_CHOL_TRAIL, F_QAPPLY, F_CHART_PANEL,
-  F_CHART_TRAIL, F_CLOSURE, F_COUNT
+  F_CHART_TRAIL, F_CLOSURE, F_SMALL, F_COUNT
 };
 
 static std::atomic<long long> g_launches{0};
@@ -85,6 +86,8 @@ struct Prof {
   } while (0)
 
 constexpr int kMaxN = 4096;
+constexpr int kSmallMax = 128;   // largest order the fused one-CTA-per-matrix kernel supports
+static std::atomic<int> g_small_n{64};  // n <= g_small_n: fused kernel, no workspace
 constexpr size_t kChunkBudget = size_t(8) << 30;  // float32 working set per chunk
 constexpr int64_t kMaxChunk = 65535;              // grid.y / grid.z limit
 constexpr size_t kPanelSmemCap = 200 * 1024;
@@ -170,6 +173,17 @@ static inline bool use_rankw(int n) {
 // Output tile of the tcgen05 GEMMs: 128 x kTcBN (64 was measured slower: twice the loader work per flop).
 constexpr int kTcBN = 128;
 
+template <typename T>
+static cudaError_t small_attr() {
+  cudaError_t e = cudaFuncSetAttribute(small_qr_kernel<64, 256, T>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)small_smem_bytes<64, 256>());
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(small_qr_kernel<128, 256, T>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)small_smem_bytes<128, 256>());
+}
+
 template <class Pb>
 static cudaError_t tcx_attr() {
   return cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -242,6 +256,9 @@ static cudaError_t set_common_attrs() {
   if ((e = rwt_attr<RWTrail<float>>()) != cudaSuccess) return e;
   if ((e = rwt_attr<RWTrail<__nv_bfloat16>>()) != cudaSuccess) return e;
   if ((e = rwt_attr<RWTrail<__half>>()) != cudaSuccess) return e;
+  if ((e = small_attr<float>()) != cudaSuccess) return e;
+  if ((e = small_attr<__nv_bfloat16>()) != cudaSuccess) return e;
+  if ((e = small_attr<__half>()) != cudaSuccess) return e;
   if ((e = tcx_attr<tcx::GramX>()) != cudaSuccess) return e;
   if ((e = tcx_attr<tcx::QApplyX>()) != cudaSuccess) return e;
   return tcx_attr<tcx::ClosureX>();
@@ -336,8 +353,24 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
 }
 
 template <typename T>
+static void launch_small(const T* A, T* H, T* tau, int* info, int64_t cb, int n, cudaStream_t st,
+                         Prof* prof) {
+  QRB_LAUNCH(prof, F_SMALL,
+             if (n <= 32) small_qr_kernel<32, 128, T>
+                 <<<(unsigned)cb, 128, small_smem_bytes<32, 128>(), st>>>(A, H, tau, info, n);
+             else if (n <= 64) small_qr_kernel<64, 256, T>
+                 <<<(unsigned)cb, 256, small_smem_bytes<64, 256>(), st>>>(A, H, tau, info, n);
+             else small_qr_kernel<128, 256, T>
+                 <<<(unsigned)cb, 256, small_smem_bytes<128, 256>(), st>>>(A, H, tau, info, n));
+}
+
+template <typename T>
 static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
                              const Ws& ws, cudaStream_t st, Prof* prof) {
+  if (n <= g_small_n.load(std::memory_order_relaxed)) {  // whole pipeline, one CTA per matrix
+    launch_small<T>(A, H, tau, info, cb, n, st, prof);
+    return cudaGetLastError();
+  }
   const int nb = pick_nb(n);
   const bool tcp = use_tc(n);
   const bool rw = use_rankw(n);  // streaming rank-w tiles for every trailing update
@@ -428,6 +461,18 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
 template <typename T>
 static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
                    void* workspace, cudaStream_t st, Prof* prof) {
+  if (n <= g_small_n.load(std::memory_order_relaxed)) {
+    const Ws none{};
+    for (int64_t b0 = 0; b0 < batch; b0 += (int64_t(1) << 30)) {
+      const int64_t cnt = (batch - b0 < (int64_t(1) << 30)) ? batch - b0 : (int64_t(1) << 30);
+      const size_t nn = (size_t)n * n;
+      cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn,
+                                   static_cast<T*>(H) + b0 * nn, static_cast<T*>(tau) + b0 * n,
+                                   info + b0, cnt, n, none, st, prof);
+      if (note(e) != cudaSuccess) return QRB200_ERR_CUDA;
+    }
+    return QRB200_OK;
+  }
   const int64_t cb = chunk_of(batch, n);
   const int nb = pick_nb(n);
   const size_t need = per_chunk_bytes(cb, n, nb);
@@ -475,7 +520,7 @@ int32_t qrb200_max_n(void) { return qrb::kMaxN; }
 int qrb200_workspace_bytes(int64_t batch, int32_t n, size_t* bytes) {
   if (!bytes || batch < 0) return QRB200_ERR_INVALID_ARG;
   if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
-  if (batch == 0 || n == 0) { *bytes = 0; return QRB200_OK; }
+  if (batch == 0 || n == 0 || n <= qrb::g_small_n.load()) { *bytes = 0; return QRB200_OK; }
   const int64_t cb = qrb::chunk_of(batch, n);
   *bytes = qrb::per_chunk_bytes(cb, n, qrb::pick_nb(n));
   return QRB200_OK;
@@ -530,7 +575,8 @@ int32_t qrb200_num_families(void) { return qrb::F_COUNT; }
 const char* qrb200_family_name(int32_t family) {
   static const char* names[qrb::F_COUNT] = {"lu_panel",    "lu_trail",    "gram",
                                             "chol_panel",  "chol_trail",  "q_apply",
-                                            "chart_panel", "chart_trail", "closure"};
+                                            "chart_panel", "chart_trail", "closure",
+                                            "small_fused"};
   return (family >= 0 && family < qrb::F_COUNT) ? names[family] : "unknown";
 }
 
@@ -540,6 +586,11 @@ int qrb200_set_option(int32_t key, int64_t value) {
   if (key == QRB200_OPT_GEMM_PATH) {
     if (value < 0 || value > 2) return QRB200_ERR_INVALID_ARG;
     qrb::g_gemm_path.store((int)value);
+    return QRB200_OK;
+  }
+  if (key == QRB200_OPT_SMALL_N) {
+    if (value < 0 || value > qrb::kSmallMax) return QRB200_ERR_INVALID_ARG;
+    qrb::g_small_n.store((int)value);
     return QRB200_OK;
   }
   return QRB200_ERR_INVALID_ARG;

@@ -128,6 +128,7 @@ int qrbt_qapply(const float* X, const float* RL, const float* D, float* Q, int* 
 
 // ---- panel phase timing (built with QRB_PANEL_TIMERS) ----
 #include "qrb_panel_reg.cuh"
+#include "qrb_small.cuh"
 
 template <int MODE>
 static int panel_timing_impl(const float* src, int64_t batch, int n, int k0, int w, int reg,
@@ -173,4 +174,26 @@ extern "C" int qrbt_panel_timing(int mode, const float* src, int64_t batch, int 
   if (mode == 0) return panel_timing_impl<PM_PIVOT>(src, batch, n, k0, w, reg, cycles_out, ms_out);
   if (mode == 1) return panel_timing_impl<PM_CHOL>(src, batch, n, k0, w, reg, cycles_out, ms_out);
   return panel_timing_impl<PM_CHART>(src, batch, n, k0, w, reg, cycles_out, ms_out);
+}
+
+// fused small-n kernel: one launch over `batch` matrices, CTA 0's phase cycles
+extern "C" int qrbt_small_timing(const float* A, float* H, float* tau, int* info, int64_t batch,
+                                 int n, long long* cycles_out, float* ms_out) {
+  auto launch = [&]() {
+    if (n <= 32) small_qr_kernel<32, 128, float><<<(unsigned)batch, 128, small_smem_bytes<32, 128>()>>>(A, H, tau, info, n);
+    else if (n <= 64) small_qr_kernel<64, 256, float><<<(unsigned)batch, 256, small_smem_bytes<64, 256>()>>>(A, H, tau, info, n);
+    else small_qr_kernel<128, 256, float><<<(unsigned)batch, 256, small_smem_bytes<128, 256>()>>>(A, H, tau, info, n);
+  };
+  cudaFuncSetAttribute(small_qr_kernel<64, 256, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)small_smem_bytes<64, 256>());
+  cudaFuncSetAttribute(small_qr_kernel<128, 256, float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)small_smem_bytes<128, 256>());
+  launch();
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0); cudaEventCreate(&e1);
+  cudaEventRecord(e0);
+  launch();
+  cudaEventRecord(e1);
+  cudaEventSynchronize(e1);
+  cudaEventElapsedTime(ms_out, e0, e1);
+  cudaMemcpyFromSymbol(cycles_out, g_panel_timers, 8 * sizeof(long long));
+  return (int)cudaGetLastError();
 }

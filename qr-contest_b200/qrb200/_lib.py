@@ -28,6 +28,7 @@ INFO_LU_ZERO_PIVOT = 8
 INFO_DEVICE_TIMEOUT = 16
 
 OPT_GEMM_PATH = 1
+OPT_SMALL_N = 2
 GEMM_AUTO, GEMM_SIMT, GEMM_TC = 0, 1, 2
 
 # every symbol include/qrb200.h declares, with its ctypes signature
@@ -127,5 +128,12 @@ def geqrf_batched_timed(A_ptr, H_ptr, tau_ptr, info_ptr, batch, n, dtype, ws_ptr
 def set_gemm_path(path: int) -> None:
     """0 = automatic, 1 = SIMT tiles only, 2 = tcgen05 tiles whenever n % 4 == 0."""
     rc = lib().qrb200_set_option(OPT_GEMM_PATH, int(path))
+    if rc != QRB200_OK:
+        raise QRB200Error(rc, "qrb200_set_option")
+
+
+def set_small_n(n_max: int) -> None:
+    """Largest order handled by the fused one-CTA-per-matrix kernel (0..128)."""
+    rc = lib().qrb200_set_option(OPT_SMALL_N, int(n_max))
     if rc != QRB200_OK:
         raise QRB200Error(rc, "qrb200_set_option")

@@ -40,9 +40,12 @@ def test_version_and_limits():
 def test_workspace_bytes():
     assert _lib.workspace_bytes(0, 64) == 0
     assert _lib.workspace_bytes(10, 0) == 0
-    a = _lib.workspace_bytes(1, 64)
-    b = _lib.workspace_bytes(2, 64)
-    assert 5 * 64 * 64 * 4 <= a < b
+    # n <= 64 (default) runs the fused one-CTA-per-matrix kernel: no workspace at all
+    assert _lib.workspace_bytes(1000, 64) == 0 and _lib.workspace_bytes(7, 32) == 0
+    assert _lib.workspace_bytes(7, 128) > 0
+    a = _lib.workspace_bytes(1, 200)
+    b = _lib.workspace_bytes(2, 200)
+    assert 5 * 200 * 200 * 4 <= a < b
     # n=512, batch 1536 fits one chunk: >= 5 float32 n x n buffers per matrix
     assert _lib.workspace_bytes(1536, 512) >= 1536 * 5 * 512 * 512 * 4
     with pytest.raises(_lib.QRB200Error):
@@ -65,7 +68,7 @@ def test_argument_validation_without_gpu():
     assert _call(dtype=9) == _lib.QRB200_ERR_INVALID_ARG
     assert _call(A=None) == _lib.QRB200_ERR_INVALID_ARG
     assert _call(info=None) == _lib.QRB200_ERR_INVALID_ARG
-    assert _call(ws=1, wsb=16) == _lib.QRB200_ERR_WORKSPACE
+    assert _call(n=200, ws=1, wsb=16) == _lib.QRB200_ERR_WORKSPACE
     # empty problems are a successful no-op
     assert _call(batch=0, A=None, H=None, tau=None, info=None) == _lib.QRB200_OK
     assert _call(n=0) == _lib.QRB200_OK
@@ -87,3 +90,18 @@ def test_library_has_no_torch_dependency():
                          text=True, check=True).stdout
     needed = [l for l in out.splitlines() if "NEEDED" in l]
     assert needed and not any(("torch" in l) or ("c10" in l) for l in needed), needed
+
+
+def test_small_n_option():
+    with pytest.raises(_lib.QRB200Error):
+        _lib.set_small_n(129)
+    with pytest.raises(_lib.QRB200Error):
+        _lib.set_small_n(-1)
+    try:
+        _lib.set_small_n(128)
+        assert _lib.workspace_bytes(7, 128) == 0
+        _lib.set_small_n(0)
+        assert _lib.workspace_bytes(7, 16) > 0
+    finally:
+        _lib.set_small_n(64)
+    assert _lib.workspace_bytes(7, 64) == 0

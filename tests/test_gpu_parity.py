@@ -186,3 +186,20 @@ def test_large_n_gates(n):
     torch.cuda.synchronize()
     assert int(info.abs().sum()) == 0
     assert_gates(A, H, tau, f"n={n}")
+
+
+@pytest.mark.parametrize("small_n", [0, 128])
+@pytest.mark.parametrize("n", [16, 64, 96, 128])
+def test_fused_and_staged_paths(small_n, n):
+    """Both sides of the fused/staged crossover on the same inputs: small_n=0 forces the staged
+    kernels at every n, small_n=128 the fused one-CTA-per-matrix kernel up to n=128."""
+    from qrb200 import _lib, generators as G
+    A = G.heterogeneous(12, n, seed=33, device="cpu")
+    _lib.set_small_n(small_n)
+    try:
+        H, tau = run(A)
+    finally:
+        _lib.set_small_n(64)
+    assert_gates(A, H, tau, f"small_n={small_n} n={n}")
+    Ho, to = O.custom_kernel_np(A.numpy())
+    assert_tight(H[:2], tau[:2], Ho[:2], to[:2])
