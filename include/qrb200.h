@@ -126,6 +126,21 @@ const char* qrb200_last_cuda_error(void);
 int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, int32_t* info,
                                  int64_t batch, int32_t n, int32_t dtype, void* stream);
 
+/* Host-buffer variant: A, H, tau and info are HOST pointers (page-locked memory gives
+ * overlapped copies; pageable memory works without the overlap).  Replaces the reference's
+ * `custom_kernel(data)` called on a CPU tensor (reflection_no_reflectors.py:181-196), whose
+ * results come back in host memory when the call returns.  The batch is cut into sub-batches
+ * of `sub_batch` matrices (0 = automatic) that rotate over three streams: upload, factor and
+ * download of neighbouring sub-batches overlap.  Device buffers are allocated on first use,
+ * cached per device and grown as needed (qrb200_release_host_staging frees them).  The
+ * sub-batches wait for work already queued on `stream`; the call blocks until every result
+ * is in host memory.  Same results, status codes and info bits as qrb200_geqrf_batched. */
+int qrb200_geqrf_batched_host(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
+                              int32_t n, int32_t dtype, int64_t sub_batch, void* stream);
+
+/* Frees the current device's cached buffers of qrb200_geqrf_batched_host. */
+int qrb200_release_host_staging(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -696,3 +696,134 @@ extern "C" int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, i
     default: return qrb::run_noalloc<__half>(A, H, tau, info, batch, n, scratch, cb, st);
   }
 }
+
+// ---------------------------------------------------------------------------------------
+// Host-buffer entry point.
+//
+// A, H, tau and info live in host memory.  The batch is cut into sub-batches that rotate
+// over kHostSlots streams; each slot owns device copies of its sub-batch's A/H/tau/info and
+// its own workspace, and runs  upload -> factor -> download  in stream order.  Sub-batch i's
+// kernels therefore overlap the upload of i+1 and the download of i-1 (the two copy
+// directions run on separate copy engines), and kernels of neighbouring slots overlap each
+// other, which keeps the one-CTA-per-matrix panel stages busy.  With page-locked host
+// buffers the copies are asynchronous; pageable buffers give the same results without the
+// overlap.  The device buffers are cached per device and only ever grow; they are released
+// by qrb200_release_host_staging.
+// ---------------------------------------------------------------------------------------
+namespace qrb {
+
+constexpr int kHostSlots = 3;
+
+struct HostStaging {
+  void* base = nullptr;
+  size_t bytes = 0;
+};
+static std::mutex g_host_mu;
+static HostStaging g_host_staging[128];
+
+static int64_t host_sub_batch(int64_t batch, int n) {
+  // six sub-batches keep the exposed first upload / last download at about 1/6 of one copy
+  // direction; at least 2 matrices per SM per sub-batch so each stage still fills the GPU
+  const int64_t floor_cnt = n <= g_small_n.load() ? 4096 : (n <= 256 ? 1184 : 296);
+  int64_t sb = (batch + 5) / 6;
+  if (sb < floor_cnt) sb = floor_cnt;
+  return sb < batch ? sb : batch;
+}
+
+}  // namespace qrb
+
+extern "C" int qrb200_geqrf_batched_host(const void* A, void* H, void* tau, int32_t* info,
+                                         int64_t batch, int32_t n, int32_t dtype,
+                                         int64_t sub_batch, void* stream) {
+  using namespace qrb;
+  if (batch < 0 || sub_batch < 0) return QRB200_ERR_INVALID_ARG;
+  if (n < 0 || n > kMaxN) return QRB200_ERR_UNSUPPORTED_N;
+  if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
+    return QRB200_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB200_OK;
+  if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
+  const size_t es = dtype == QRB200_F32 ? 4 : 2;
+  const int64_t sb = sub_batch > 0 ? (sub_batch < batch ? sub_batch : batch)
+                                   : host_sub_batch(batch, n);
+  const size_t nn = (size_t)n * n;
+  size_t ws_bytes = 0;
+  int rc = qrb200_workspace_bytes(sb, n, &ws_bytes);
+  if (rc != QRB200_OK) return rc;
+  const size_t a_b = align256(sb * nn * es), t_b = align256(sb * n * es),
+               i_b = align256(sb * sizeof(int32_t)), w_b = align256(ws_bytes);
+  const size_t slot_bytes = 2 * a_b + t_b + i_b + w_b;
+
+  int dev = 0;
+  if (note(cudaGetDevice(&dev)) != cudaSuccess) return QRB200_ERR_CUDA;
+  if (dev < 0 || dev >= 128) return QRB200_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_host_mu);
+  HostStaging& hs = g_host_staging[dev];
+  const size_t need = kHostSlots * slot_bytes;
+  if (hs.bytes < need) {
+    if (hs.base && note(cudaFree(hs.base)) != cudaSuccess) return QRB200_ERR_CUDA;
+    hs.base = nullptr;
+    hs.bytes = 0;
+    if (note(cudaMalloc(&hs.base, need)) != cudaSuccess) return QRB200_ERR_CUDA;
+    hs.bytes = need;
+  }
+  cudaStream_t caller = static_cast<cudaStream_t>(stream);
+  cudaStream_t st[kHostSlots] = {};
+  cudaEvent_t start = nullptr;
+  auto cleanup = [&](int r) {
+    for (int s = 0; s < kHostSlots; ++s)
+      if (st[s]) {
+        if (cudaStreamSynchronize(st[s]) != cudaSuccess && r == QRB200_OK) r = QRB200_ERR_CUDA;
+        cudaStreamDestroy(st[s]);
+      }
+    if (start) cudaEventDestroy(start);
+    return r;
+  };
+  if (note(cudaEventCreateWithFlags(&start, cudaEventDisableTiming)) != cudaSuccess ||
+      note(cudaEventRecord(start, caller)) != cudaSuccess)
+    return cleanup(QRB200_ERR_CUDA);
+  for (int s = 0; s < kHostSlots; ++s)
+    if (note(cudaStreamCreateWithFlags(&st[s], cudaStreamNonBlocking)) != cudaSuccess ||
+        note(cudaStreamWaitEvent(st[s], start, 0)) != cudaSuccess)
+      return cleanup(QRB200_ERR_CUDA);
+
+  const char* hA = static_cast<const char*>(A);
+  char* hH = static_cast<char*>(H);
+  char* hT = static_cast<char*>(tau);
+  int64_t j = 0;
+  for (int64_t b0 = 0; b0 < batch; b0 += sb, ++j) {
+    const int64_t cnt = batch - b0 < sb ? batch - b0 : sb;
+    const int s = (int)(j % kHostSlots);
+    char* base = static_cast<char*>(hs.base) + s * slot_bytes;
+    void* dA = base;
+    void* dH = base + a_b;
+    void* dT = base + 2 * a_b;
+    int32_t* dI = reinterpret_cast<int32_t*>(base + 2 * a_b + t_b);
+    void* dW = ws_bytes ? base + 2 * a_b + t_b + i_b : nullptr;
+    if (note(cudaMemcpyAsync(dA, hA + b0 * nn * es, cnt * nn * es, cudaMemcpyHostToDevice,
+                             st[s])) != cudaSuccess)
+      return cleanup(QRB200_ERR_CUDA);
+    rc = geqrf_impl(dA, dH, dT, dI, cnt, n, dtype, dW, ws_bytes, st[s], nullptr);
+    if (rc != QRB200_OK) return cleanup(rc);
+    if (note(cudaMemcpyAsync(hH + b0 * nn * es, dH, cnt * nn * es, cudaMemcpyDeviceToHost,
+                             st[s])) != cudaSuccess ||
+        note(cudaMemcpyAsync(hT + b0 * n * es, dT, cnt * n * es, cudaMemcpyDeviceToHost,
+                             st[s])) != cudaSuccess ||
+        note(cudaMemcpyAsync(info + b0, dI, cnt * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                             st[s])) != cudaSuccess)
+      return cleanup(QRB200_ERR_CUDA);
+  }
+  return cleanup(QRB200_OK);
+}
+
+extern "C" int qrb200_release_host_staging(void) {
+  using namespace qrb;
+  int dev = 0;
+  if (note(cudaGetDevice(&dev)) != cudaSuccess) return QRB200_ERR_CUDA;
+  if (dev < 0 || dev >= 128) return QRB200_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_host_mu);
+  HostStaging& hs = g_host_staging[dev];
+  if (hs.base && note(cudaFree(hs.base)) != cudaSuccess) return QRB200_ERR_CUDA;
+  hs.base = nullptr;
+  hs.bytes = 0;
+  return QRB200_OK;
+}

@@ -57,6 +57,11 @@ SIGNATURES = {
                                                     ctypes.c_void_p, ctypes.c_void_p,
                                                     ctypes.c_int64, ctypes.c_int32,
                                                     ctypes.c_int32, ctypes.c_void_p]),
+    "qrb200_geqrf_batched_host": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
+                                                 ctypes.c_void_p, ctypes.c_void_p,
+                                                 ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                                 ctypes.c_int64, ctypes.c_void_p]),
+    "qrb200_release_host_staging": (ctypes.c_int, []),
 }
 
 _LIB = None

@@ -10,9 +10,12 @@
   ``torch.linalg.LinAlgError``, as ``torch.linalg.cholesky`` does at :76 (NaN/Inf input
   ends there too).
 
-Differences that come from the hardware contract: the tensor must live on a CUDA device
-(there is no CPU path), and float32 / bfloat16 / float16 are read and written natively by
-the kernels; any other dtype is converted to float32 on the device first.
+The tensor may live on a CUDA device (results stay there) or in host memory (results come
+back in host memory, like the reference called on a CPU tensor).  Host tensors are factored
+on the current CUDA device through ``qrb200_geqrf_batched_host``, which overlaps the copies
+with the kernels (page-locked tensors give the overlap).  There is no CPU compute path: without
+a CUDA device or the compiled library the call raises.  float32 / bfloat16 / float16 are read
+and written natively by the kernels; any other dtype is converted to float32 first.
 """
 from __future__ import annotations
 
@@ -31,9 +34,8 @@ def _prep(data: torch.Tensor):
         raise TypeError("custom_kernel expects a torch.Tensor")
     if data.dim() < 2 or data.shape[-1] != data.shape[-2]:
         raise ValueError(f"expected a (..., n, n) tensor, got shape {tuple(data.shape)}")
-    if data.device.type != "cuda":
-        raise ValueError("qrb200 runs on CUDA devices only (got a tensor on "
-                         f"{data.device}); there is no CPU fallback")
+    if data.device.type not in ("cuda", "cpu"):
+        raise ValueError(f"qrb200 takes CUDA or host tensors (got one on {data.device})")
     A = data if data.dtype in _NATIVE else data.to(torch.float32)
     return A.contiguous()
 
@@ -51,6 +53,8 @@ def geqrf(data: torch.Tensor, workspace: torch.Tensor | None = None):
     :func:`workspace_bytes` bytes; when omitted one is taken from torch's caching allocator.
     """
     A = _prep(data)
+    if A.device.type == "cpu":
+        return geqrf_host(data)
     lead, n = A.shape[:-2], A.shape[-1]
     batch = 1
     for d in lead:
@@ -71,6 +75,44 @@ def geqrf(data: torch.Tensor, workspace: torch.Tensor | None = None):
                                     need, stream)
         if rc != _lib.QRB200_OK:
             raise _lib.QRB200Error(rc, "qrb200_geqrf_batched")
+    if data.dtype not in _NATIVE:
+        H, tau = H.to(data.dtype), tau.to(data.dtype)
+    return H, tau, info
+
+
+def geqrf_host(data: torch.Tensor, out=None, sub_batch: int = 0):
+    """Factor a HOST tensor on the current CUDA device; returns host ``(H, tau, info)``.
+
+    Blocking.  ``out`` = optional preallocated host ``(H, tau, info)`` (page-locked tensors
+    let the library overlap the copies with the kernels); ``sub_batch`` = matrices per
+    pipelined sub-batch, 0 for the library's choice.
+    """
+    A = _prep(data)
+    if A.device.type != "cpu":
+        raise ValueError("geqrf_host takes a host tensor")
+    lead, n = A.shape[:-2], A.shape[-1]
+    batch = 1
+    for d in lead:
+        batch *= int(d)
+    if out is None:
+        H = torch.empty_like(A)
+        tau = torch.empty(*lead, n, dtype=A.dtype)
+        info = torch.zeros(*lead, dtype=torch.int32)
+    else:
+        H, tau, info = out
+        if (H.shape != A.shape or H.dtype != A.dtype or tau.shape != (*lead, n)
+                or tau.dtype != A.dtype or info.shape != lead or info.dtype != torch.int32
+                or not (H.is_contiguous() and tau.is_contiguous() and info.is_contiguous())
+                or H.device.type != "cpu" or tau.device.type != "cpu"
+                or info.device.type != "cpu"):
+            raise ValueError("out must be contiguous host (H, tau, info) matching the input")
+    if batch > 0 and n > 0:
+        stream = torch.cuda.current_stream().cuda_stream
+        rc = _lib.lib().qrb200_geqrf_batched_host(A.data_ptr(), H.data_ptr(), tau.data_ptr(),
+                                                   info.data_ptr(), batch, n,
+                                                   _NATIVE[A.dtype], int(sub_batch), stream)
+        if rc != _lib.QRB200_OK:
+            raise _lib.QRB200Error(rc, "qrb200_geqrf_batched_host")
     if data.dtype not in _NATIVE:
         H, tau = H.to(data.dtype), tau.to(data.dtype)
     return H, tau, info

@@ -171,9 +171,33 @@ def test_info_clean_on_valid_input():
     assert int(info.abs().sum()) == 0
 
 
-def test_cpu_tensor_rejected():
-    with pytest.raises(ValueError):
-        qrb().custom_kernel(torch.randn(2, 4, 4))
+@pytest.mark.parametrize("n,b,sub", [(16, 40, 7), (96, 30, 0), (200, 11, 4), (256, 9, 2)])
+def test_host_buffers_match_device_path(n, b, sub):
+    """qrb200_geqrf_batched_host (host tensors, pipelined sub-batches over three streams)
+    returns exactly what the device entry point returns for the same matrices."""
+    from qrb200 import generators as G
+    A = G.heterogeneous(b, n, seed=41, device="cpu")
+    Hd, td, infod = qrb().geqrf(A.cuda())
+    torch.cuda.synchronize()
+    out = (torch.empty_like(A).pin_memory(), torch.empty(b, n).pin_memory(),
+           torch.full((b,), -1, dtype=torch.int32).pin_memory())
+    H, tau, info = qrb().api.geqrf_host(A.pin_memory(), out=out, sub_batch=sub)
+    assert H.device.type == "cpu" and H.data_ptr() == out[0].data_ptr()
+    assert torch.equal(H, Hd.cpu()) and torch.equal(tau, td.cpu())
+    assert torch.equal(info, infod.cpu())
+    assert_gates(A, H, tau, f"host n={n}")
+
+
+def test_host_custom_kernel_pageable_and_dtypes():
+    A = torch.randn(3, 2, 40, 40, generator=torch.Generator().manual_seed(5))
+    H, tau = qrb().custom_kernel(A)                       # pageable host tensor
+    assert H.device.type == "cpu" and H.shape == A.shape and tau.shape == (3, 2, 40)
+    Hd, td = qrb().custom_kernel(A.cuda())
+    assert torch.equal(H, Hd.cpu()) and torch.equal(tau, td.cpu())
+    H64, t64 = qrb().custom_kernel(A.double())            # converted like .to(float32)
+    assert H64.dtype == torch.float64 and torch.equal(H64.float(), H)
+    Hb, tb = qrb().custom_kernel(A.to(torch.bfloat16))
+    assert Hb.dtype == torch.bfloat16 and Hb.device.type == "cpu"
 
 
 @pytest.mark.parametrize("n", [1040, 2048])
