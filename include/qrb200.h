@@ -99,6 +99,16 @@ long long qrb200_launch_count(void);
  *   the whole pipeline of one matrix in one CTA's shared memory (no workspace); larger n use
  *   the staged kernels.  Changing it also changes qrb200_workspace_bytes. */
 #define QRB200_OPT_SMALL_N 2
+/*   QRB200_OPT_CHOL_BLOCK: column block of the two-level Cholesky elimination of the
+ *   CholeskyQR passes (0 = one level: every 32-wide panel updates the whole trailing matrix;
+ *   64, 128 (default) or 256: the panels update only their block and the rest of the trailing
+ *   matrix takes one K = block update per block).  Used when the tcgen05 path is active and
+ *   n > block.  qrb200_workspace_bytes reflects the value set when it is called. */
+#define QRB200_OPT_CHOL_BLOCK 3
+/*   QRB200_OPT_LANES: number of internal streams (1..4, default 2) a chunk of the batch is
+ *   split over; they fork from and join back to the caller's stream, so the call keeps its
+ *   stream semantics.  1 = everything on the caller's stream. */
+#define QRB200_OPT_LANES 4
 int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return

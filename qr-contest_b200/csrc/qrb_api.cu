@@ -91,6 +91,8 @@ static std::atomic<int> g_small_n{64};  // n <= g_small_n: fused kernel, no work
 constexpr size_t kChunkBudget = size_t(8) << 30;  // float32 working set per chunk
 constexpr int64_t kMaxChunk = 65535;              // grid.y / grid.z limit
 constexpr size_t kPanelSmemCap = 200 * 1024;
+// column block of the two-level Cholesky elimination (QRB200_OPT_CHOL_BLOCK; 0 = one level)
+static std::atomic<int> g_chol_block{128};
 
 static int pick_nb(int n) {
   for (int w = 32; w >= 8; w >>= 1)
@@ -99,6 +101,16 @@ static int pick_nb(int n) {
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+// Carving the workspace into per-lane parts costs at most 13 x 256 bytes of alignment each.
+constexpr size_t kLaneSlack = 4 * 13 * 256;
+
+// Columns of the W / Wc panel buffers (rows of Bp): the panels of one Cholesky column block
+// keep theirs side by side when the two-level elimination runs (nb = 32, n > kCholBlock).
+static int ws_cols(int n) {
+  const int nb = pick_nb(n);
+  const int cb = g_chol_block.load(std::memory_order_relaxed);
+  return (nb == 32 && cb > 0 && n > cb) ? cb : nb;
+}
 
 struct Ws {
   float *T0, *T1, *L, *R, *Q1, *W, *s, *mu, *D, *Wc, *Bp;
@@ -118,7 +130,7 @@ static size_t per_chunk_bytes(int64_t cb, int n, int nbmax) {
 }
 
 static int64_t chunk_of(int64_t batch, int n) {
-  const size_t per = per_chunk_bytes(1, n, 32);
+  const size_t per = per_chunk_bytes(1, n, ws_cols(n));
   int64_t c = (int64_t)(kChunkBudget / per);
   if (c < 1) c = 1;
   if (c > kMaxChunk) c = kMaxChunk;
@@ -245,6 +257,7 @@ static cudaError_t set_common_attrs() {
   if ((e = tc_attr<tc::GramTC>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::QApplyTC>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::SyrkTC>()) != cudaSuccess) return e;
+  if ((e = tc_attr<tc::LinvBlkTC>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::ClosureTC<float>>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::ClosureTC<__nv_bfloat16>>()) != cudaSuccess) return e;
   if ((e = tc_attr<tc::ClosureTC<__half>>()) != cudaSuccess) return e;
@@ -314,32 +327,58 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   if (tcp && pass2)
     QRB_LAUNCH(prof, F_GRAM,
                colnorm2_kernel<<<dim3((n + 255) / 256, (unsigned)cb), 256, 0, st>>>(X, ws.T0, n));
-  for (int k0 = 0; k0 < n; k0 += nb) {
-    const int w = (n - k0 < nb) ? n - k0 : nb;
-    PanelArgs pa{};
-    pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
-    pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = ws.W; pa.Wc = ws.Wc; pa.Bp = ws.Bp;
-    pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
-    QRB_LAUNCH(prof, F_CHOL_PANEL,
-               (launch_panel<PM_CHOL, float, float>(pa, cb, st)));
-    const int k1 = k0 + w;
-    if (k1 < n)
+  // Two-level blocking: the 32-wide panels of a column block [kb, ke) update only the block
+  // (its columns for every row below, and the L_G^{-1} rows inside it); the rest of the
+  // trailing triangle and the L_G^{-1} rows below the block then take one update with
+  // K = ke - kb (SyrkTC and LinvBlkTC), which moves the trailing matrix once per block
+  // instead of once per panel.  The panels of a block keep their W / Wc columns and their
+  // L_G^{-1} row snapshots side by side (ldw = the block width).
+  const int cblk = g_chol_block.load(std::memory_order_relaxed);
+  const bool blk = tcp && rw && nb == 32 && cblk > 0 && n > cblk;
+  const int ldw = blk ? cblk : nb;
+  for (int kb = 0; kb < n; kb += (blk ? cblk : n)) {
+    const int ke = blk ? (n - kb < cblk ? n : kb + cblk) : n;
+    for (int k0 = kb; k0 < ke; k0 += nb) {
+      const int w = (n - k0 < nb) ? n - k0 : nb;
+      const int jo = blk ? k0 - kb : 0;  // this panel's column / row offset in W, Wc, Bp
+      float* Wp = ws.W + jo;
+      float* Wcp = ws.Wc + jo;
+      float* Bpp = ws.Bp + (size_t)jo * n;
+      PanelArgs pa{};
+      pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = ldw;
+      pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = Wp; pa.Wc = Wcp; pa.Bp = Bpp;
+      pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
+      QRB_LAUNCH(prof, F_CHOL_PANEL,
+                 (launch_panel<PM_CHOL, float, float>(pa, cb, st)));
+      const int k1 = k0 + w;
+      if (k1 < ke)
+        QRB_LAUNCH(prof, F_CHOL_TRAIL,
+                   if (tcp && rw) tc::tc_rankw_kernel<RWSyrk>
+                       <<<rwt_grid(n - k1, ke - k1, cb), 256, tc::RWT_SMEM, st>>>(
+                           RWSyrkArgs{n, k0, k1, ldw, ws.T0, ws.R, Wcp, info, ke});
+                   else if (rw) rankw_kernel<RWSyrk><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                       RWSyrkArgs{n, k0, k1, ldw, ws.T0, ws.R, Wcp, info, n});
+                   else simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                       TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 if (tcp && rw) tc::tc_rankw_kernel<RWSyrk>
-                     <<<rwt_grid(n - k1, n - k1, cb), 256, tc::RWT_SMEM, st>>>(
-                         RWSyrkArgs{n, k0, k1, nb, ws.T0, ws.R, ws.Wc, info});
-                 else if (rw) rankw_kernel<RWSyrk><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
-                     RWSyrkArgs{n, k0, k1, nb, ws.T0, ws.R, ws.Wc, info});
-                 else simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
-                     TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
-    QRB_LAUNCH(prof, F_CHOL_TRAIL,
-               if (tcp && rw) tc::tc_rankw_kernel<RWLinv>
-                   <<<rwt_grid(n - k0, k1, cb), 256, tc::RWT_SMEM, st>>>(
-                       RWLinvArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp, info});
-               else if (rw) rankw_kernel<RWLinv><<<rw_grid(n - k0, k1, cb), 256, 0, st>>>(
-                   RWLinvArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp, info});
-               else simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k0, k1, cb), 256, 0, st>>>(
-                   LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp}));
+                 if (tcp && rw) tc::tc_rankw_kernel<RWLinv>
+                     <<<rwt_grid(ke - k0, k1, cb), 256, tc::RWT_SMEM, st>>>(
+                         RWLinvArgs{n, k0, k1, ldw, ws.R, Wp, Bpp, info, ke});
+                 else if (rw) rankw_kernel<RWLinv><<<rw_grid(n - k0, k1, cb), 256, 0, st>>>(
+                     RWLinvArgs{n, k0, k1, ldw, ws.R, Wp, Bpp, info, n});
+                 else simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k0, k1, cb), 256, 0, st>>>(
+                     LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp}));
+    }
+    if (ke < n) {
+      QRB_LAUNCH(prof, F_CHOL_TRAIL,
+                 tc::tc_gemm_kernel<tc::SyrkTC, kTcBN><<<tc_grid(n - ke, n - ke, cb), tc::NTHREADS,
+                                                         kTcSmem, st>>>(
+                     tc::SyrkTCArgs{n, kb, ke, ws.T0, ws.R, info}));
+      QRB_LAUNCH(prof, F_CHOL_TRAIL,
+                 tc::tc_gemm_kernel<tc::LinvBlkTC, kTcBN><<<tc_grid(n - ke, ke, cb), tc::NTHREADS,
+                                                           kTcSmem, st>>>(
+                     tc::LinvBlkArgs{n, kb, ke, ldw, ws.R, ws.W, ws.Bp, info}));
+    }
   }
   const QApplyArgs qa{n, pass2 ? 1 : 0, X, ws.R, ws.D, Q, info};
   tcx::Maps qm;
@@ -458,6 +497,25 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   return cudaGetLastError();
 }
 
+// Internal streams of the lane split (created once per device, never destroyed).
+constexpr int kMaxLanes = 4;
+static std::atomic<int> g_lanes{2};  // QRB200_OPT_LANES
+static cudaStream_t* lane_streams() {
+  static std::mutex mu;
+  static cudaStream_t lanes[128][kMaxLanes];
+  static bool made[128] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  std::lock_guard<std::mutex> g(mu);
+  if (!made[dev]) {
+    for (int l = 0; l < kMaxLanes; ++l)
+      if (note(cudaStreamCreateWithFlags(&lanes[dev][l], cudaStreamNonBlocking)) != cudaSuccess)
+        return nullptr;
+    made[dev] = true;
+  }
+  return lanes[dev];
+}
+
 template <typename T>
 static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
                    void* workspace, cudaStream_t st, Prof* prof) {
@@ -475,7 +533,7 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
   }
   const int64_t cb = chunk_of(batch, n);
   const int nb = pick_nb(n);
-  const size_t need = per_chunk_bytes(cb, n, nb);
+  const size_t need = per_chunk_bytes(cb, n, ws_cols(n)) + kLaneSlack;
   void* ws = workspace;
   bool owned = false;
   if (!ws) {
@@ -484,11 +542,43 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
   }
   int rc = QRB200_OK;
   const size_t nn = (size_t)n * n;
+  const int cols = ws_cols(n);
+  const int L = prof ? 1 : g_lanes.load(std::memory_order_relaxed);
+  cudaStream_t* lane = (L > 1) ? lane_streams() : nullptr;
   for (int64_t b0 = 0; b0 < batch; b0 += cb) {
     const int64_t cnt = (batch - b0 < cb) ? batch - b0 : cb;
-    const Ws w = carve(ws, cnt, n, nb);
-    cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
-                                 static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof);
+    if (!lane || cnt < 2 * L) {
+      const Ws w = carve(ws, cnt, n, cols);
+      cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
+                                   static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof);
+      if (note(e) != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
+      continue;
+    }
+    // Lanes: the chunk's matrices are independent, so sub-batches run on L internal streams
+    // forked from and joined back to the caller's stream.  The latency-bound panels of one
+    // sub-batch then overlap the bandwidth-bound trailing updates of another.
+    cudaEvent_t fork = nullptr, join[kMaxLanes] = {};
+    cudaError_t e = cudaEventCreateWithFlags(&fork, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventRecord(fork, st);
+    char* p = static_cast<char*>(ws);
+    const int64_t per = (cnt + L - 1) / L;
+    for (int l = 0; l < L && e == cudaSuccess; ++l) {
+      const int64_t s0 = l * per, c = (cnt - s0 < per) ? cnt - s0 : per;
+      if (c <= 0) break;
+      e = cudaStreamWaitEvent(lane[l], fork, 0);
+      if (e != cudaSuccess) break;
+      const Ws w = carve(p, c, n, cols);
+      p += per_chunk_bytes(c, n, cols);
+      const int64_t o = b0 + s0;
+      e = run_chunk<T>(static_cast<const T*>(A) + o * nn, static_cast<T*>(H) + o * nn,
+                       static_cast<T*>(tau) + o * n, info + o, c, n, w, lane[l], nullptr);
+      if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join[l], cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventRecord(join[l], lane[l]);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(st, join[l], 0);
+    }
+    if (fork) cudaEventDestroy(fork);
+    for (int l = 0; l < L; ++l)
+      if (join[l]) cudaEventDestroy(join[l]);
     if (note(e) != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
   }
   if (owned && note(cudaFreeAsync(ws, st)) != cudaSuccess) rc = QRB200_ERR_CUDA;
@@ -522,7 +612,7 @@ int qrb200_workspace_bytes(int64_t batch, int32_t n, size_t* bytes) {
   if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
   if (batch == 0 || n == 0 || n <= qrb::g_small_n.load()) { *bytes = 0; return QRB200_OK; }
   const int64_t cb = qrb::chunk_of(batch, n);
-  *bytes = qrb::per_chunk_bytes(cb, n, qrb::pick_nb(n));
+  *bytes = qrb::per_chunk_bytes(cb, n, qrb::ws_cols(n)) + qrb::kLaneSlack;
   return QRB200_OK;
 }
 
@@ -586,6 +676,16 @@ int qrb200_set_option(int32_t key, int64_t value) {
   if (key == QRB200_OPT_GEMM_PATH) {
     if (value < 0 || value > 2) return QRB200_ERR_INVALID_ARG;
     qrb::g_gemm_path.store((int)value);
+    return QRB200_OK;
+  }
+  if (key == QRB200_OPT_LANES) {
+    if (value < 1 || value > qrb::kMaxLanes) return QRB200_ERR_INVALID_ARG;
+    qrb::g_lanes.store((int)value);
+    return QRB200_OK;
+  }
+  if (key == QRB200_OPT_CHOL_BLOCK) {
+    if (value != 0 && value != 64 && value != 128 && value != 256) return QRB200_ERR_INVALID_ARG;
+    qrb::g_chol_block.store((int)value);
     return QRB200_OK;
   }
   if (key == QRB200_OPT_SMALL_N) {
@@ -659,11 +759,11 @@ static int64_t noalloc_chunk(int n, int nb) {
 template <typename T>
 static int run_noalloc(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
                        void* scratch, int64_t cb, cudaStream_t st) {
-  const int nb = pick_nb(n);
+  const int cols = ws_cols(n);
   const size_t nn = (size_t)n * n;
   for (int64_t b0 = 0; b0 < batch; b0 += cb) {
     const int64_t cnt = (batch - b0 < cb) ? batch - b0 : cb;
-    const Ws w = carve(scratch, cnt, n, nb);
+    const Ws w = carve(scratch, cnt, n, cols);
     cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
                                  static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st,
                                  nullptr);
@@ -683,7 +783,7 @@ extern "C" int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, i
     return QRB200_ERR_INVALID_ARG;
   if (batch == 0 || n == 0) return QRB200_OK;
   if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
-  const int64_t cb = qrb::noalloc_chunk(n, qrb::pick_nb(n));
+  const int64_t cb = qrb::noalloc_chunk(n, qrb::ws_cols(n));
   if (cb < 1) return QRB200_ERR_SCRATCH_LIMIT;
   if (qrb::note(qrb::ensure_attrs()) != cudaSuccess) return QRB200_ERR_CUDA;
   void* scratch = nullptr;

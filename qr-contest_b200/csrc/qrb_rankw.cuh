@@ -151,12 +151,14 @@ struct RWSyrkArgs {
   const float* R;   // rows [k0, k1): R12 = D^{1/2} L21^T
   const float* Wc;  // rows [k1, n): L21 D^{1/2}
   int* info;
+  int lim;          // columns [k1, lim) are updated (n: the whole trailing triangle)
 };
 struct RWSyrk {
   using Args = RWSyrkArgs;
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
-    M = N = a.n - a.k1;
+    M = a.n - a.k1;
+    N = a.lim - a.k1;
     K = a.k1 - a.k0;
   }
   __device__ static bool live(const Args&, int m0, int n0) { return n0 < m0 + RW_M; }
@@ -188,12 +190,13 @@ struct RWLinvArgs {
   const float* Wl;  // rows [k0, n): L11^{-1} then W
   const float* Bp;  // [ldw][n] per matrix: raw panel rows, columns [0, k1)
   int* info;
+  int lim;          // rows [k0, lim) are updated (n: every row below the panel)
 };
 struct RWLinv {
   using Args = RWLinvArgs;
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
-    M = a.n - a.k0;
+    M = a.lim - a.k0;
     N = a.k1;
     K = a.k1 - a.k0;
   }

@@ -237,6 +237,85 @@ struct SyrkTC {
 };
 
 // ---------------------------------------------------------------------------------------
+// L_G^{-1} update of a whole column block [kb, ke) of the Cholesky elimination, for the rows
+// below the block (the block's panels updated only the rows inside it):
+//   Linv[r][j] = C_in[r][j] - sum_p W_p[r] B_p[j],   r in [ke, n), j < ke,
+// with W_p = L21 L11^{-1} of panel p (column block [kb + 32p, kb + 32p + 32) of the W buffer)
+// and B_p = the panel's rows of L_G^{-1} just before that panel (rows [32p, 32p + 32) of the Bp
+// buffer, identity block included, zero from the panel's end column on).  C_in is Linv[r][j]
+// for j < kb and 0 on the block's own columns.  The sum over the block's panels is the product
+// of the stacked operands, one GEMM with K = ke - kb.
+struct LinvBlkArgs {
+  int n, kb, ke, ldw;
+  float* RL;
+  const float* W;   // [n][ldw] per matrix
+  const float* Bp;  // [ldw][n] per matrix
+  int* info;
+};
+struct LinvBlkTC {
+  using Args = LinvBlkArgs;
+  static constexpr bool A_ALONG_K = true, B_ALONG_K = false;
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) {
+    M = a.n - a.ke;
+    N = a.ke;
+    K = a.ke - a.kb;
+  }
+  __device__ static bool live(int, int, int, int) { return true; }
+  __device__ static void krange(const Args& a, int, int, int& kb, int& ke) {
+    kb = 0;
+    ke = a.ke - a.kb;
+  }
+  __device__ static void loadA(const Args& a, int64_t b, int m0, int k0, float (&v)[4][4]) {
+    const int M = a.n - a.ke, K = a.ke - a.kb;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      if (m0 + i < M)
+        ld4(a.W + ((int64_t)b * a.n + a.ke + m0 + i) * a.ldw + k0, clamp4(K - k0),
+            (a.ldw & 3) == 0, o);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) v[i][kk] = o[kk];
+    }
+  }
+  __device__ static void loadB(const Args& a, int64_t b, int j0, int k0, float (&v)[4][4]) {
+    ld_rows_k(a.Bp + (int64_t)b * a.ldw * a.n, a.n, j0, clamp4(a.ke - j0), k0,
+              clamp4(a.ke - a.kb - k0), (a.n & 3) == 0, v);
+  }
+  // row k of B belongs to panel k / 32, whose snapshot ends at column kb + 32 (k / 32 + 1)
+  __device__ static void fixB(const Args& a, int64_t, int j0, int k0, float (&v)[4][4]) {
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int jend = a.kb + 32 * ((k0 + kk) / 32 + 1);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (j0 + i >= jend) v[i][kk] = 0.f;
+    }
+  }
+  __device__ static void store(const Args& a, int64_t b, int m, int j0, const float* v, int,
+                               int N) {
+    float* row = a.RL + mat_off(b, a.n) + (int64_t)(a.ke + m) * a.n;
+    float o[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const int j = j0 + i;
+      float t[4] = {0.f, 0.f, 0.f, 0.f};
+      if (j + 3 < a.kb && (a.n & 3) == 0) {
+        const float4 c = *reinterpret_cast<const float4*>(row + j);
+        t[0] = c.x; t[1] = c.y; t[2] = c.z; t[3] = c.w;
+      } else {
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (j + u < a.kb) t[u] = row[j + u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o[i + u] = t[u] - v[i + u];
+    }
+    st_row32(row + j0, o, N - j0, (a.n & 3) == 0);
+  }
+  __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
+};
+
+// ---------------------------------------------------------------------------------------
 // R^{-1} application of one CholeskyQR pass (see QApply in qrb_gemm_simt.cuh):
 // B(k, j) = R^{-1}[k][j] (pass 1) or (I - R^{-1})[k][j] (pass 2), built in the loader from
 // row j of L_G^{-1} (contiguous in k) and d_j; the k range of column tile [n0, n0+BN) stops

@@ -29,6 +29,8 @@ INFO_DEVICE_TIMEOUT = 16
 
 OPT_GEMM_PATH = 1
 OPT_SMALL_N = 2
+OPT_CHOL_BLOCK = 3
+OPT_LANES = 4
 GEMM_AUTO, GEMM_SIMT, GEMM_TC = 0, 1, 2
 
 # every symbol include/qrb200.h declares, with its ctypes signature
@@ -140,5 +142,19 @@ def set_gemm_path(path: int) -> None:
 def set_small_n(n_max: int) -> None:
     """Largest order handled by the fused one-CTA-per-matrix kernel (0..128)."""
     rc = lib().qrb200_set_option(OPT_SMALL_N, int(n_max))
+    if rc != QRB200_OK:
+        raise QRB200Error(rc, "qrb200_set_option")
+
+
+def set_chol_block(block: int) -> None:
+    """Column block of the two-level Cholesky elimination: 0 (one level), 64, 128 or 256."""
+    rc = lib().qrb200_set_option(OPT_CHOL_BLOCK, int(block))
+    if rc != QRB200_OK:
+        raise QRB200Error(rc, "qrb200_set_option")
+
+
+def set_lanes(lanes: int) -> None:
+    """Internal streams a chunk of the batch is split over (1..4)."""
+    rc = lib().qrb200_set_option(OPT_LANES, int(lanes))
     if rc != QRB200_OK:
         raise QRB200Error(rc, "qrb200_set_option")

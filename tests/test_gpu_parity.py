@@ -227,3 +227,42 @@ def test_fused_and_staged_paths(small_n, n):
     assert_gates(A, H, tau, f"small_n={small_n} n={n}")
     Ho, to = O.custom_kernel_np(A.numpy())
     assert_tight(H[:2], tau[:2], Ho[:2], to[:2])
+
+
+@pytest.mark.parametrize("block", [0, 64, 256])
+@pytest.mark.parametrize("n", [192, 320, 512])
+def test_cholesky_block_widths(block, n):
+    """The two-level Cholesky elimination at every block width (0 = one level: every panel
+    updates the whole trailing matrix) against the default width on the same inputs: gates on
+    all six classes, tight agreement on the well-determined classes."""
+    from qrb200 import _lib, generators as G
+    A = G.heterogeneous(12, n, seed=41, device="cuda")
+    H0, t0 = run(A)
+    _lib.set_chol_block(block)
+    try:
+        H, tau = run(A)
+    finally:
+        _lib.set_chol_block(128)
+    assert_gates(A, H, tau, f"block={block} n={n}")
+    assert_tight(H[:2], tau[:2], H0[:2].cpu().numpy(), t0[:2].cpu().numpy())
+
+
+@pytest.mark.parametrize("lanes", [1, 3, 4])
+def test_lanes_bit_identical(lanes):
+    """Splitting a chunk over internal streams changes only the schedule: every matrix is
+    factored by the same kernels, so H, tau and info match the default (2 lanes) bit for bit,
+    and the call still completes in the caller's stream order."""
+    from qrb200 import _lib, generators as G
+    A = G.heterogeneous(37, 256, seed=43, device="cuda")
+    H0, t0, i0 = qrb().geqrf(A)
+    _lib.set_lanes(lanes)
+    try:
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            H, tau, info = qrb().geqrf(A)
+            Hc = H.clone()  # ordered after the factorization on the caller's stream
+        torch.cuda.synchronize()
+    finally:
+        _lib.set_lanes(2)
+    assert torch.equal(H, H0) and torch.equal(Hc, H0)
+    assert torch.equal(tau, t0) and torch.equal(info, i0)
