@@ -316,7 +316,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   tcx::Maps gm;
   const bool gx = tcp && tcx_maps(gm, X, false, X, false, n, cb);
   QRB_LAUNCH(prof, F_GRAM,
-             if (gx) tcx::tcx_gemm_kernel<tcx::GramX><<<tc_grid(n, n, cb), tc::NTHREADS,
+             if (gx) tcx::tcx_gemm_kernel<tcx::GramX><<<tc_grid(n, n, cb), tcx::XTHREADS,
                                                         tcx::SMEM_BYTES, st>>>(
                  gm, tc::GramTCArgs{n, X, ws.T0, info});
              else if (tcp) tc::tc_gemm_kernel<tc::GramTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
@@ -384,7 +384,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   tcx::Maps qm;
   const bool qx = tcp && tcx_maps(qm, X, true, ws.R, true, n, cb);
   QRB_LAUNCH(prof, F_QAPPLY,
-             if (qx) tcx::tcx_gemm_kernel<tcx::QApplyX><<<tc_grid(n, n, cb), tc::NTHREADS,
+             if (qx) tcx::tcx_gemm_kernel<tcx::QApplyX><<<tc_grid(n, n, cb), tcx::XTHREADS,
                                                           tcx::SMEM_BYTES, st>>>(qm, qa);
              else if (tcp) tc::tc_gemm_kernel<tc::QApplyTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                 kTcSmem, st>>>(qa);
@@ -486,7 +486,7 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   tcx::Maps cm;
   const bool cx = tcp && std::is_same<T, float>::value && tcx_maps(cm, ws.L, false, A, false, n, cb);
   QRB_LAUNCH(prof, F_CLOSURE,
-             if (cx) tcx::tcx_gemm_kernel<tcx::ClosureX><<<tc_grid(n, n, cb), tc::NTHREADS,
+             if (cx) tcx::tcx_gemm_kernel<tcx::ClosureX><<<tc_grid(n, n, cb), tcx::XTHREADS,
                                                            tcx::SMEM_BYTES, st>>>(
                  cm, tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
              else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>

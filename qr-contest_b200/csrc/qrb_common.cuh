@@ -13,6 +13,11 @@
 
 namespace qrb {
 
+#ifdef QRB_PANEL_TIMERS
+// phase-timer slots of the test kit's profiling build (off in the library)
+__device__ long long g_panel_timers[8];
+#endif
+
 enum Dtype : int { DT_F32 = 0, DT_BF16 = 1, DT_F16 = 2 };
 
 // Per-matrix status bits written into info[b] (0 = clean).

@@ -28,7 +28,6 @@
 
 // Phase timers for the test kit's profiling build only (off in the library).
 #ifdef QRB_PANEL_TIMERS
-__device__ long long g_panel_timers[8];
 #define QRB_PT(i)                                                         \
   do {                                                                    \
     __syncthreads();                                                      \

@@ -35,6 +35,13 @@ __device__ __forceinline__ float tf32_rn(float x) {
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
   return __uint_as_float(r);
 }
+// Same rounding (to nearest, ties away from zero) on the integer pipe: add half of the 13
+// dropped mantissa bits to the bit pattern, then clear them.  A carry out of the mantissa
+// bumps the exponent, which is the correctly rounded result.  Finite inputs below the
+// largest binade only (all operands here are).
+__device__ __forceinline__ float tf32_rn_int(float x) {
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
+}
 
 // ---- mbarrier ----
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
@@ -135,10 +142,10 @@ __device__ __forceinline__ void put4x4(char* hi, char* lo, int r0, int kchunk,
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     float4 h, l;
-    h.x = tf32_rn(v[i][0]); l.x = tf32_rn(v[i][0] - h.x);
-    h.y = tf32_rn(v[i][1]); l.y = tf32_rn(v[i][1] - h.y);
-    h.z = tf32_rn(v[i][2]); l.z = tf32_rn(v[i][2] - h.z);
-    h.w = tf32_rn(v[i][3]); l.w = tf32_rn(v[i][3] - h.w);
+    h.x = tf32_rn_int(v[i][0]); l.x = tf32_rn_int(v[i][0] - h.x);
+    h.y = tf32_rn_int(v[i][1]); l.y = tf32_rn_int(v[i][1] - h.y);
+    h.z = tf32_rn_int(v[i][2]); l.z = tf32_rn_int(v[i][2] - h.z);
+    h.w = tf32_rn_int(v[i][3]); l.w = tf32_rn_int(v[i][3] - h.w);
     const uint32_t off = sw128_off(r0 + i, kchunk);
     *reinterpret_cast<float4*>(hi + off) = h;
     *reinterpret_cast<float4*>(lo + off) = l;

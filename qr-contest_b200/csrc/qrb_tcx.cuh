@@ -88,8 +88,34 @@ __device__ __forceinline__ void read_raw(const char* raw, int rb, int kc, float 
 
 // Policy additions over the tc_ops policies: A_KMAJOR / B_KMAJOR (raw layout of the sources
 // described by the two tensor maps), fixA (elementwise transform of an A block, may be empty).
+#ifdef QRB_PANEL_TIMERS
+// test-kit profiling build: cycle sums per phase over all CTAs, of split thread 0 (slots 0-3)
+// and of the issuing thread (slots 4-5)
+#define QRB_GT(who, i)                                                     \
+  do {                                                                     \
+    if (tid == (who)) {                                                    \
+      const long long now_ = clock64();                                    \
+      atomicAdd(reinterpret_cast<unsigned long long*>(&g_panel_timers[i]), \
+                (unsigned long long)(now_ - gt_prev_));                    \
+      gt_prev_ = now_;                                                     \
+    }                                                                      \
+  } while (0)
+#else
+#define QRB_GT(who, i) do { } while (0)
+#endif
+
+// Warp roles: warps 0-7 split raw tiles into hi/lo planes and run the epilogue; warp 8 (one
+// elected lane) issues the TMA loads and the MMAs.  tcgen05.mma issue blocks while the tensor
+// pipe works through the previous stage, so the issuing thread must not be one the split waits
+// for: with a CTA-wide barrier per stage the split, the waits and the MMAs ran back to back.
+// Hand-offs are mbarriers only:
+//   full[s]     TMA -> split      raw tiles of stage t landed          (tx bytes)
+//   pfull[ps]   split -> issuer   planes of stage t written            (256 arrivals)
+//   mma_bar[ps] MMAs -> split     planes of stage t free / TMEM ready  (tcgen05.commit)
+constexpr int XTHREADS = NTHREADS + 32;
+
 template <class Pb>
-__global__ void __launch_bounds__(NTHREADS, 1)
+__global__ void __launch_bounds__(XTHREADS, 1)
     tcx_gemm_kernel(const __grid_constant__ Maps maps, typename Pb::Args a) {
   extern __shared__ __align__(1024) char smraw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
@@ -98,7 +124,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   char* pl0 = sm + RAW_STAGES * (RAW_A + RAW_B);    // [PLANE_SETS] x {a_hi, a_lo, b_hi, b_lo}
   uint64_t* full = reinterpret_cast<uint64_t*>(pl0 + PLANE_SETS * 4 * PLANE);  // [RAW_STAGES]
   uint64_t* mma_bar = full + RAW_STAGES;                                          // [PLANE_SETS]
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mma_bar + PLANE_SETS);
+  uint64_t* pfull = mma_bar + PLANE_SETS;                                         // [PLANE_SETS]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(pfull + PLANE_SETS);
 
   const int64_t b = blockIdx.z;
   const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
@@ -110,6 +137,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   Pb::krange(a, m0, n0, kb, ke);
   const int nk = (ke > kb) ? (ke - kb + BK - 1) / BK : 0;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool issuer_warp = warp == NTHREADS / 32;
+#ifdef QRB_PANEL_TIMERS
+  long long gt_prev_ = clock64();
+#endif
 
   if (warp == 0) {
     tc::tmem_alloc(tslot, BN);
@@ -117,25 +148,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   if (tid == 0) {
     for (int s = 0; s < RAW_STAGES; ++s) tc::mbar_init(&full[s], 1);
-    for (int p = 0; p < PLANE_SETS; ++p) tc::mbar_init(&mma_bar[p], 1);
+    for (int p = 0; p < PLANE_SETS; ++p) {
+      tc::mbar_init(&mma_bar[p], 1);
+      tc::mbar_init(&pfull[p], NTHREADS);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // per-column scale of the B transform (QApplyX: d_j^{-1/2}), read once per tile
+  __shared__ float tscale[BN];
+  if constexpr (Pb::TILE_SCALE)
+    for (int j = tid; j < BN; j += XTHREADS) tscale[j] = Pb::col_scale(a, b, n0 + j);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
   const uint32_t tmem = *tslot;
-
-  auto issue = [&](int t) {  // producer: raw tiles of k-step t into slot t % RAW_STAGES
-    const int s = t % RAW_STAGES, k0 = kb + t * BK;
-    mbar_expect_tx(&full[s], RAW_A + RAW_B);
-    issue_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, &maps.a, m0, k0, (int)b, &full[s]);
-    issue_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, &maps.b, n0, k0, (int)b, &full[s]);
-  };
-  if (tid == 0) {
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
-    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
-    for (int t = 0; t < nk && t < RAW_STAGES; ++t) issue(t);
-  }
 
   // Long reductions drain the TMEM accumulator into float32 registers every DRAIN stages:
   // TMEM accumulation does not round to nearest on each add, and over K = 2048 the drift is
@@ -146,69 +172,99 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
   for (int i = 0; i < BN / 2; ++i) racc[i] = 0.f;
   const int lq = warp & 3;
-
-  const int a_mb = tid >> 3, a_kc = tid & 7;   // A: 32 row blocks x 8 k chunks
-  const int b_jb = tid >> 3, b_kc = tid & 7;   // B: 32 column blocks x 8 k chunks
-  constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
   bool ok = true;
-  for (int t = 0; t < nk; ++t) {
-    const int s = t % RAW_STAGES, k0 = kb + t * BK;
-    const int ps = t & 1;                 // plane set of this stage
-    char* pl = pl0 + ps * 4 * PLANE;
-    if (!tc::mbar_wait(&full[s], (t / RAW_STAGES) & 1)) ok = false;
-    // plane set ps was last read by the MMAs of stage t-2 (commit number t/2 - 1 on mma_bar[ps])
-    if (t >= 2 && !tc::mbar_wait(&mma_bar[ps], ((t >> 1) - 1) & 1)) ok = false;
-    float v[4][4];
-    read_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, a_mb, a_kc, v);
-    Pb::fixA(a, b, m0 + 4 * a_mb, k0 + 4 * a_kc, v);
-    tc::put4x4(pl, pl + PLANE, 4 * a_mb, a_kc, v);
-    read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, b_jb, b_kc, v);
-    Pb::fixB(a, b, n0 + 4 * b_jb, k0 + 4 * b_kc, v);
-    tc::put4x4(pl + 2 * PLANE, pl + 3 * PLANE, 4 * b_jb, b_kc, v);
-    tc::fence_async_smem();
-    tc::tc_fence_before();
-    __syncthreads();
-    if (tid == 0) {
-      tc::tc_fence_after();
-      if (t + RAW_STAGES < nk) issue(t + RAW_STAGES);  // slot s has been read by everyone
-      const uint32_t ah = tc::smem_u32(pl), al = tc::smem_u32(pl + PLANE);
-      const uint32_t bh = tc::smem_u32(pl + 2 * PLANE), bl = tc::smem_u32(pl + 3 * PLANE);
-#pragma unroll
-      for (int kk = 0; kk < BK / UK; ++kk) {
-        const uint32_t koff = kk * UK * 4;
-        const uint64_t dah = tc::sdesc_sw128(ah + koff), dal = tc::sdesc_sw128(al + koff);
-        const uint64_t dbh = tc::sdesc_sw128(bh + koff), dbl = tc::sdesc_sw128(bl + koff);
-        const bool fresh = (drains ? (t % DRAIN == 0) : (t == 0)) && kk == 0;
-        tc::mma_tf32(tmem, dal, dbh, IDESC, fresh ? 0u : 1u);
-        tc::mma_tf32(tmem, dah, dbl, IDESC, 1u);
-        tc::mma_tf32(tmem, dah, dbh, IDESC, 1u);
-      }
-      tc::mma_commit(&mma_bar[ps]);
-    }
-    if (drains && (t + 1) % DRAIN == 0 && t + 1 < nk) {
-      if (!tc::mbar_wait(&mma_bar[ps], (t >> 1) & 1)) ok = false;
-      tc::tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < BN / 2; c += 32) {
-        float v[32];
-        tc::tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + (warp >> 2) * (BN / 2) + c, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) racc[c + i] += v[i];
-      }
-      tc::tc_fence_before();
-      __syncthreads();
-    }
-  }
-  // the last commit covers every MMA issued before it
-  if (nk >= 1) {
-    const int t = nk - 1;
-    if (!tc::mbar_wait(&mma_bar[t & 1], (t >> 1) & 1)) ok = false;
-  }
-  tc::tc_fence_after();
 
-  if (!ok) {
-    if (tid == 0) atomicOr(Pb::info(a, b), INFO_DEVICE_TIMEOUT);
+  if (issuer_warp) {
+    if (lane == 0) {
+      auto issue = [&](int t) {  // raw tiles of k-step t into slot t % RAW_STAGES
+        const int s = t % RAW_STAGES, k0 = kb + t * BK;
+        mbar_expect_tx(&full[s], RAW_A + RAW_B);
+        issue_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, &maps.a, m0, k0, (int)b, &full[s]);
+        issue_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, &maps.b, n0, k0, (int)b, &full[s]);
+      };
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
+      for (int t = 0; t < nk && t < RAW_STAGES; ++t) issue(t);
+      constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
+      for (int t = 0; t < nk; ++t) {
+        const int ps = t & 1;
+        char* pl = pl0 + ps * 4 * PLANE;
+        if (ok && !tc::mbar_wait(&pfull[ps], (t >> 1) & 1)) ok = false;
+        tc::tc_fence_after();
+        QRB_GT(NTHREADS, 4);
+        if (t + RAW_STAGES < nk) issue(t + RAW_STAGES);  // slot t % RAW_STAGES has been split
+        const uint32_t ah = tc::smem_u32(pl), al = tc::smem_u32(pl + PLANE);
+        const uint32_t bh = tc::smem_u32(pl + 2 * PLANE), bl = tc::smem_u32(pl + 3 * PLANE);
+#pragma unroll
+        for (int kk = 0; kk < BK / UK; ++kk) {
+          const uint32_t koff = kk * UK * 4;
+          const uint64_t dah = tc::sdesc_sw128(ah + koff), dal = tc::sdesc_sw128(al + koff);
+          const uint64_t dbh = tc::sdesc_sw128(bh + koff), dbl = tc::sdesc_sw128(bl + koff);
+          const bool fresh = (drains ? (t % DRAIN == 0) : (t == 0)) && kk == 0;
+          tc::mma_tf32(tmem, dal, dbh, IDESC, fresh ? 0u : 1u);
+          tc::mma_tf32(tmem, dah, dbl, IDESC, 1u);
+          tc::mma_tf32(tmem, dah, dbh, IDESC, 1u);
+        }
+        tc::mma_commit(&mma_bar[ps]);
+        QRB_GT(NTHREADS, 5);
+      }
+    }
   } else {
+    // Split mapping: 32 row blocks x 8 k chunks, one micro-block per thread.  The 8 threads of
+    // a quarter-warp take row blocks 8g + q and k chunks (q + c) % 8 (q = 0..7): their 16-byte
+    // accesses then fall on 8 distinct bank groups both when they read a raw tile stored
+    // m-major (chunk q ^ 4(kc & 1)) or k-major, and when they write the swizzled planes.
+    const int sq = tid & 7, sg = tid >> 3;
+    const int a_mb = 8 * (sg & 3) + sq, a_kc = (sq + (sg >> 2)) & 7;
+    const int b_jb = a_mb, b_kc = a_kc;
+    QRB_GT(0, 0);
+    for (int t = 0; t < nk; ++t) {
+      const int s = t % RAW_STAGES, k0 = kb + t * BK;
+      const int ps = t & 1;                 // plane set of this stage
+      char* pl = pl0 + ps * 4 * PLANE;
+      if (ok && !tc::mbar_wait(&full[s], (t / RAW_STAGES) & 1)) ok = false;
+      QRB_GT(0, 1);
+      // plane set ps was last read by the MMAs of stage t-2 (commit t/2 - 1 on mma_bar[ps])
+      if (t >= 2 && ok && !tc::mbar_wait(&mma_bar[ps], ((t >> 1) - 1) & 1)) ok = false;
+      QRB_GT(0, 2);
+      float v[4][4];
+      read_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, a_mb, a_kc, v);
+      Pb::fixA(a, b, m0 + 4 * a_mb, k0 + 4 * a_kc, v);
+      tc::put4x4(pl, pl + PLANE, 4 * a_mb, a_kc, v);
+      read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, b_jb, b_kc, v);
+      if constexpr (Pb::TILE_SCALE)
+        Pb::fixB_scaled(a, n0 + 4 * b_jb, k0 + 4 * b_kc, tscale + 4 * b_jb, v);
+      else
+        Pb::fixB(a, b, n0 + 4 * b_jb, k0 + 4 * b_kc, v);
+      tc::put4x4(pl + 2 * PLANE, pl + 3 * PLANE, 4 * b_jb, b_kc, v);
+      tc::fence_async_smem();   // generic-proxy plane writes -> visible to the MMAs
+      tc::tc_fence_before();    // orders this thread's earlier tcgen05.ld (drain) too
+      asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&pfull[ps]))
+                   : "memory");
+      QRB_GT(0, 3);
+      if (drains && (t + 1) % DRAIN == 0 && t + 1 < nk) {
+        if (ok && !tc::mbar_wait(&mma_bar[ps], (t >> 1) & 1)) ok = false;
+        tc::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < BN / 2; c += 32) {
+          float v2[32];
+          tc::tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + (warp >> 2) * (BN / 2) + c, v2);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) racc[c + i] += v2[i];
+        }
+      }
+    }
+    // the last commit covers every MMA issued before it
+    if (nk >= 1 && ok) {
+      const int t = nk - 1;
+      if (!tc::mbar_wait(&mma_bar[t & 1], (t >> 1) & 1)) ok = false;
+    }
+    tc::tc_fence_after();
+  }
+
+  if (__syncthreads_or(!ok)) {
+    if (tid == 0) atomicOr(Pb::info(a, b), INFO_DEVICE_TIMEOUT);
+  } else if (!issuer_warp) {
     const int m = m0 + 32 * lq + lane;
     constexpr int CPW = BN / 2;
 #pragma unroll
@@ -227,20 +283,44 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   tc::tc_fence_before();
   __syncthreads();
+  QRB_GT(0, 6);
   if (warp == 0) tc::tmem_dealloc(tmem, BN);
 }
 
 // ---- policies: the tc_ops ones plus the raw-layout flags ----
 struct GramX : tc::GramTC {
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // X[k][m], X[k][j]
+  static constexpr bool TILE_SCALE = false;
   __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 struct QApplyX : tc::QApplyTC {
   static constexpr bool A_KMAJOR = true, B_KMAJOR = true;    // X[m][k], RL[j][k]
+  static constexpr bool TILE_SCALE = true;
   __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
+  __device__ static float col_scale(const Args& a, int64_t b, int j) {
+    return (j < a.n) ? 1.f / sqrtf(a.D[b * a.n + j]) : 0.f;
+  }
+  // QApplyTC::fixB with d_j^{-1/2} from the tile's shared copy (rs[i] for column j0 + i)
+  __device__ static void fixB_scaled(const Args& a, int j0, int k0, const float* rs,
+                                     float (&v)[4][4]) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int j = j0 + i;
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int k = k0 + kk;
+        float r;
+        if (j >= a.n || k > j) r = 0.f;
+        else if (k < j) r = a.pass2 ? -(v[i][kk] * rs[i]) : v[i][kk] * rs[i];
+        else r = a.pass2 ? (1.f - rs[i]) : rs[i];
+        v[i][kk] = r;
+      }
+    }
+  }
 };
 struct ClosureX : tc::ClosureTC<float> {
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // Q[k][m], A[k][j]
+  static constexpr bool TILE_SCALE = false;
   __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 

@@ -30,7 +30,7 @@ static int tcx_launch(const void* a, bool ak, const void* b, bool bk, int n, int
     return 999;
   cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        tcx::SMEM_BYTES);
-  tcx::tcx_gemm_kernel<Pb><<<g128(n, n, batch), 256, tcx::SMEM_BYTES, s>>>(mp, args);
+  tcx::tcx_gemm_kernel<Pb><<<g128(n, n, batch), tcx::XTHREADS, tcx::SMEM_BYTES, s>>>(mp, args);
   return 0;
 }
 
@@ -194,6 +194,27 @@ extern "C" int qrbt_small_timing(const float* A, float* H, float* tau, int* info
   cudaEventRecord(e1);
   cudaEventSynchronize(e1);
   cudaEventElapsedTime(ms_out, e0, e1);
+  cudaMemcpyFromSymbol(cycles_out, g_panel_timers, 8 * sizeof(long long));
+  return (int)cudaGetLastError();
+}
+
+// Phase cycle sums (thread 0, all CTAs) of the TMA-fed Gram tile over `batch` n x n matrices:
+// prologue, wait raw, wait planes free, split, barrier, issue, epilogue; plus the launch time.
+extern "C" int qrbt_tcx_timing(const float* X, float* G, int* info, int64_t batch, int n,
+                               long long* cycles_out, float* ms_out) {
+  cudaStream_t s = 0;
+  if (int e = tcx_launch<tcx::GramX>(X, false, X, false, n, batch, tc::GramTCArgs{n, X, G, info}, s))
+    return e;
+  long long zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  cudaMemcpyToSymbol(g_panel_timers, zero, sizeof(zero));
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0); cudaEventCreate(&e1);
+  cudaEventRecord(e0);
+  tcx_launch<tcx::GramX>(X, false, X, false, n, batch, tc::GramTCArgs{n, X, G, info}, s);
+  cudaEventRecord(e1);
+  cudaEventSynchronize(e1);
+  cudaEventElapsedTime(ms_out, e0, e1);
+  cudaEventDestroy(e0); cudaEventDestroy(e1);
   cudaMemcpyFromSymbol(cycles_out, g_panel_timers, 8 * sizeof(long long));
   return (int)cudaGetLastError();
 }
