@@ -199,14 +199,14 @@ static cudaError_t small_attr() {
 template <class Pb>
 static cudaError_t tcx_attr() {
   return cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              tcx::SMEM_BYTES);
+                              tcx::smem_bytes<Pb>());
 }
 
 // TMA maps for a tcx launch: operands stored k-major use 128-row boxes, m-major 32-row boxes.
 static bool tcx_maps(tcx::Maps& mp, const void* a, bool a_kmajor, const void* b, bool b_kmajor,
                      int n, int64_t cb) {
-  return encode_batched(&mp.a, a, n, cb, a_kmajor ? 128 : 32) &&
-         encode_batched(&mp.b, b, n, cb, b_kmajor ? 128 : 32);
+  return (a_kmajor ? encode_batched(&mp.a, a, n, cb, 128) : encode_batched_wide(&mp.a, a, n, cb)) &&
+         (b_kmajor ? encode_batched(&mp.b, b, n, cb, 128) : encode_batched_wide(&mp.b, b, n, cb));
 }
 
 template <class Pb>
@@ -317,7 +317,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   const bool gx = tcp && tcx_maps(gm, X, false, X, false, n, cb);
   QRB_LAUNCH(prof, F_GRAM,
              if (gx) tcx::tcx_gemm_kernel<tcx::GramX><<<tc_grid(n, n, cb), tcx::XTHREADS,
-                                                        tcx::SMEM_BYTES, st>>>(
+                                                        tcx::smem_bytes<tcx::GramX>(), st>>>(
                  gm, tc::GramTCArgs{n, X, ws.T0, info});
              else if (tcp) tc::tc_gemm_kernel<tc::GramTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                kTcSmem, st>>>(
@@ -385,7 +385,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   const bool qx = tcp && tcx_maps(qm, X, true, ws.R, true, n, cb);
   QRB_LAUNCH(prof, F_QAPPLY,
              if (qx) tcx::tcx_gemm_kernel<tcx::QApplyX><<<tc_grid(n, n, cb), tcx::XTHREADS,
-                                                          tcx::SMEM_BYTES, st>>>(qm, qa);
+                                                          tcx::smem_bytes<tcx::QApplyX>(), st>>>(qm, qa);
              else if (tcp) tc::tc_gemm_kernel<tc::QApplyTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                 kTcSmem, st>>>(qa);
              else simt_gemm_kernel<QApply><<<tiles_grid(n, n, cb), 256, 0, st>>>(qa));
@@ -487,7 +487,7 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   const bool cx = tcp && std::is_same<T, float>::value && tcx_maps(cm, ws.L, false, A, false, n, cb);
   QRB_LAUNCH(prof, F_CLOSURE,
              if (cx) tcx::tcx_gemm_kernel<tcx::ClosureX><<<tc_grid(n, n, cb), tcx::XTHREADS,
-                                                           tcx::SMEM_BYTES, st>>>(
+                                                           tcx::smem_bytes<tcx::ClosureX>(), st>>>(
                  cm, tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
              else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>
                  <<<tc_grid(n, n, cb), tc::NTHREADS, kTcSmem, st>>>(

@@ -25,12 +25,21 @@ using tc::NTHREADS;
 using tc::UK;
 
 constexpr int BN = 128;
-constexpr int RAW_STAGES = 3;
+#ifndef QRB_TCX_STAGES
+#define QRB_TCX_STAGES 3
+#endif
+constexpr int RAW_STAGES = QRB_TCX_STAGES;  // raw tiles in flight (3 measured best of 3-5)
 constexpr int RAW_A = BM * BK * 4;   // 16 KB
 constexpr int RAW_B = BN * BK * 4;   // 16 KB
 constexpr int PLANE = 16384;         // one hi or lo plane of a 128 x 32 operand tile
 constexpr int PLANE_SETS = 2;      // split of stage t+1 overlaps the MMAs of stage t
-constexpr int SMEM_BYTES = RAW_STAGES * (RAW_A + RAW_B) + PLANE_SETS * 4 * PLANE + 1024 + 128;
+// A_TMEM policies keep A in tensor memory: a plane set holds B hi / lo only.
+template <bool A_TMEM>
+constexpr int plane_set_bytes() { return (A_TMEM ? 2 : 4) * PLANE; }
+template <class Pb>
+constexpr int smem_bytes() {
+  return RAW_STAGES * (RAW_A + RAW_B) + PLANE_SETS * plane_set_bytes<Pb::A_TMEM>() + 1024 + 128;
+}
 
 struct Maps {
   CUtensorMap a;  // raw A source
@@ -53,18 +62,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, i
 }
 
 // Raw tile of an operand whose rows (tile rows = M or N index) are contiguous in k:
-// one box {32 k, 128 rows}.  Element (r, k) sits at sw128_off(r, k/4) + 4*(k%4).
-// Raw tile of an operand stored k-major (X[k][r]): four boxes {32 r, 32 k}, box i covering
-// rows 32i..32i+31; element (r, k) at i*4096 + sw128_off(k, (r%32)/4) + 4*(r%4).
+// one box {32 k, 128 rows}, 128-byte swizzle.  Element (r, k) sits at sw128_off(r, k/4) + 4*(k%4).
+// Raw tile of an operand stored k-major (X[k][r]): one unswizzled box {128 r, 32 k}; element
+// (r, k) at 512 k + 4 r.  (Four swizzled {32, 32} boxes were measured slower: the copy engine
+// spends most of its time per box, not per byte, on these small boxes.)  The row-per-thread
+// A reads and the 4 x 4 micro-block B reads of such a tile are bank-conflict free as is.
 template <bool KMAJOR>
 __device__ __forceinline__ void issue_raw(char* dst, const CUtensorMap* map, int r0, int k0,
                                           int z, uint64_t* bar) {
-  if (KMAJOR) {
-    tma_load_3d(dst, map, k0, r0, z, bar);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) tma_load_3d(dst + i * 4096, map, r0 + 32 * i, k0, z, bar);
-  }
+  if (KMAJOR) tma_load_3d(dst, map, k0, r0, z, bar);
+  else tma_load_3d(dst, map, r0, k0, z, bar);
 }
 
 // 4(row) x 4(k) micro-block (rows 4*rb.., k 4*kc..) out of a raw tile.
@@ -77,17 +84,17 @@ __device__ __forceinline__ void read_raw(const char* raw, int rb, int kc, float 
       v[i][0] = t.x; v[i][1] = t.y; v[i][2] = t.z; v[i][3] = t.w;
     }
   } else {
-    const char* blk = raw + (rb >> 3) * 4096;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      const float4 t = *reinterpret_cast<const float4*>(blk + tc::sw128_off(4 * kc + kk, rb & 7));
+      const float4 t = *reinterpret_cast<const float4*>(raw + (4 * kc + kk) * 512 + 16 * rb);
       v[0][kk] = t.x; v[1][kk] = t.y; v[2][kk] = t.z; v[3][kk] = t.w;
     }
   }
 }
 
 // Policy additions over the tc_ops policies: A_KMAJOR / B_KMAJOR (raw layout of the sources
-// described by the two tensor maps), fixA (elementwise transform of an A block, may be empty).
+// described by the two tensor maps), TILE_SCALE (B transform with a per-column scale:
+// col_scale, fixB_scaled; otherwise fixB).
 #ifdef QRB_PANEL_TIMERS
 // test-kit profiling build: cycle sums per phase over all CTAs, of split thread 0 (slots 0-3)
 // and of the issuing thread (slots 4-5)
@@ -113,6 +120,8 @@ __device__ __forceinline__ void read_raw(const char* raw, int rb, int kc, float 
 //   pfull[ps]   split -> issuer   planes of stage t written            (256 arrivals)
 //   mma_bar[ps] MMAs -> split     planes of stage t free / TMEM ready  (tcgen05.commit)
 constexpr int XTHREADS = NTHREADS + 32;
+constexpr int TM_A = BN;              // TMEM: accumulator in columns [0, BN), A sets after it
+constexpr int TM_COLS = 256;          // BN + 2 sets x (hi, lo) x BK columns, power of two
 
 template <class Pb>
 __global__ void __launch_bounds__(XTHREADS, 1)
@@ -121,10 +130,13 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   char* rawA = sm;                                  // [RAW_STAGES][RAW_A]
   char* rawB = sm + RAW_STAGES * RAW_A;             // [RAW_STAGES][RAW_B]
-  char* pl0 = sm + RAW_STAGES * (RAW_A + RAW_B);    // [PLANE_SETS] x {a_hi, a_lo, b_hi, b_lo}
-  uint64_t* full = reinterpret_cast<uint64_t*>(pl0 + PLANE_SETS * 4 * PLANE);  // [RAW_STAGES]
+  // [PLANE_SETS] x {b_hi, b_lo} (A_TMEM) or {a_hi, a_lo, b_hi, b_lo}
+  constexpr int PSET = plane_set_bytes<Pb::A_TMEM>(), PB = Pb::A_TMEM ? 0 : 2 * PLANE;
+  char* pl0 = sm + RAW_STAGES * (RAW_A + RAW_B);
+  uint64_t* full = reinterpret_cast<uint64_t*>(pl0 + PLANE_SETS * PSET);  // [RAW_STAGES]
   uint64_t* mma_bar = full + RAW_STAGES;                                          // [PLANE_SETS]
   uint64_t* pfull = mma_bar + PLANE_SETS;                                         // [PLANE_SETS]
+  static_assert(smem_bytes<Pb>() + BN * 4 <= 227 * 1024, "tcx shared memory");
   uint32_t* tslot = reinterpret_cast<uint32_t*>(pfull + PLANE_SETS);
 
   const int64_t b = blockIdx.z;
@@ -143,7 +155,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
 #endif
 
   if (warp == 0) {
-    tc::tmem_alloc(tslot, BN);
+    tc::tmem_alloc(tslot, TM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
@@ -188,57 +200,104 @@ __global__ void __launch_bounds__(XTHREADS, 1)
       constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
       for (int t = 0; t < nk; ++t) {
         const int ps = t & 1;
-        char* pl = pl0 + ps * 4 * PLANE;
+        char* pl = pl0 + ps * PSET;
         if (ok && !tc::mbar_wait(&pfull[ps], (t >> 1) & 1)) ok = false;
         tc::tc_fence_after();
         QRB_GT(NTHREADS, 4);
         if (t + RAW_STAGES < nk) issue(t + RAW_STAGES);  // slot t % RAW_STAGES has been split
-        const uint32_t ah = tc::smem_u32(pl), al = tc::smem_u32(pl + PLANE);
-        const uint32_t bh = tc::smem_u32(pl + 2 * PLANE), bl = tc::smem_u32(pl + 3 * PLANE);
+        const uint32_t bh = tc::smem_u32(pl + PB), bl = tc::smem_u32(pl + PB + PLANE);
 #pragma unroll
         for (int kk = 0; kk < BK / UK; ++kk) {
           const uint32_t koff = kk * UK * 4;
-          const uint64_t dah = tc::sdesc_sw128(ah + koff), dal = tc::sdesc_sw128(al + koff);
           const uint64_t dbh = tc::sdesc_sw128(bh + koff), dbl = tc::sdesc_sw128(bl + koff);
           const bool fresh = (drains ? (t % DRAIN == 0) : (t == 0)) && kk == 0;
-          tc::mma_tf32(tmem, dal, dbh, IDESC, fresh ? 0u : 1u);
-          tc::mma_tf32(tmem, dah, dbl, IDESC, 1u);
-          tc::mma_tf32(tmem, dah, dbh, IDESC, 1u);
+          if constexpr (Pb::A_TMEM) {
+            const uint32_t ah = tmem + TM_A + ps * 2 * BK + kk * UK, al = ah + BK;
+            tc::mma_tf32_ta(tmem, al, dbh, IDESC, fresh ? 0u : 1u);
+            tc::mma_tf32_ta(tmem, ah, dbl, IDESC, 1u);
+            tc::mma_tf32_ta(tmem, ah, dbh, IDESC, 1u);
+          } else {
+            const uint64_t dah = tc::sdesc_sw128(tc::smem_u32(pl) + koff);
+            const uint64_t dal = tc::sdesc_sw128(tc::smem_u32(pl + PLANE) + koff);
+            tc::mma_tf32(tmem, dal, dbh, IDESC, fresh ? 0u : 1u);
+            tc::mma_tf32(tmem, dah, dbl, IDESC, 1u);
+            tc::mma_tf32(tmem, dah, dbh, IDESC, 1u);
+          }
         }
         tc::mma_commit(&mma_bar[ps]);
         QRB_GT(NTHREADS, 5);
       }
     }
   } else {
-    // Split mapping: 32 row blocks x 8 k chunks, one micro-block per thread.  The 8 threads of
-    // a quarter-warp take row blocks 8g + q and k chunks (q + c) % 8 (q = 0..7): their 16-byte
-    // accesses then fall on 8 distinct bank groups both when they read a raw tile stored
-    // m-major (chunk q ^ 4(kc & 1)) or k-major, and when they write the swizzled planes.
-    const int sq = tid & 7, sg = tid >> 3;
-    const int a_mb = 8 * (sg & 3) + sq, a_kc = (sq + (sg >> 2)) & 7;
-    const int b_jb = a_mb, b_kc = a_kc;
+    // Split roles.  Warps 0-3: thread = tile row r (its TMEM lane) of A; it reads the row's 32
+    // k values from the raw tile and writes tf32 hi / lo into the A columns of this stage's
+    // TMEM set (A never goes through shared-memory planes).  Warps 4-7: B, two 4 x 4
+    // micro-blocks per thread into the shared-memory planes; the 8 threads of a quarter-warp
+    // take column blocks 8g + q and k chunks (q + c) % 8, so their 16-byte accesses fall on 8
+    // distinct bank groups for both raw layouts and for the swizzled plane writes.
+    const bool a_role = warp < 4;
+    const int r = 32 * warp + lane;
     QRB_GT(0, 0);
     for (int t = 0; t < nk; ++t) {
       const int s = t % RAW_STAGES, k0 = kb + t * BK;
-      const int ps = t & 1;                 // plane set of this stage
-      char* pl = pl0 + ps * 4 * PLANE;
+      const int ps = t & 1;                 // plane / TMEM set of this stage
+      char* pl = pl0 + ps * PSET;
       if (ok && !tc::mbar_wait(&full[s], (t / RAW_STAGES) & 1)) ok = false;
       QRB_GT(0, 1);
-      // plane set ps was last read by the MMAs of stage t-2 (commit t/2 - 1 on mma_bar[ps])
+      // set ps was last read by the MMAs of stage t-2 (commit t/2 - 1 on mma_bar[ps])
       if (t >= 2 && ok && !tc::mbar_wait(&mma_bar[ps], ((t >> 1) - 1) & 1)) ok = false;
       QRB_GT(0, 2);
-      float v[4][4];
-      read_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, a_mb, a_kc, v);
-      Pb::fixA(a, b, m0 + 4 * a_mb, k0 + 4 * a_kc, v);
-      tc::put4x4(pl, pl + PLANE, 4 * a_mb, a_kc, v);
-      read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, b_jb, b_kc, v);
-      if constexpr (Pb::TILE_SCALE)
-        Pb::fixB_scaled(a, n0 + 4 * b_jb, k0 + 4 * b_kc, tscale + 4 * b_jb, v);
-      else
-        Pb::fixB(a, b, n0 + 4 * b_jb, k0 + 4 * b_kc, v);
-      tc::put4x4(pl + 2 * PLANE, pl + 3 * PLANE, 4 * b_jb, b_kc, v);
+      if (!Pb::A_TMEM) {
+        // all 256 threads: one A and one B micro-block each, both into shared-memory planes
+        const int sq = tid & 7, sg = tid >> 3;
+        const int mb = 8 * (sg & 3) + sq, kc = (sq + (sg >> 2)) & 7;
+        float v[4][4];
+        read_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, mb, kc, v);
+        tc::put4x4(pl, pl + PLANE, 4 * mb, kc, v);
+        read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, mb, kc, v);
+        if constexpr (Pb::TILE_SCALE)
+          Pb::fixB_scaled(a, n0 + 4 * mb, k0 + 4 * kc, tscale + 4 * mb, v);
+        else
+          Pb::fixB(a, b, n0 + 4 * mb, k0 + 4 * kc, v);
+        tc::put4x4(pl + PB, pl + PB + PLANE, 4 * mb, kc, v);
+      } else if (a_role) {
+        const char* raw = rawA + s * RAW_A;
+        float hi[BK], lo[BK];
+        if (Pb::A_KMAJOR) {
+#pragma unroll
+          for (int c = 0; c < BK / 4; ++c) {
+            const float4 x = *reinterpret_cast<const float4*>(raw + tc::sw128_off(r, c));
+            hi[4 * c] = x.x; hi[4 * c + 1] = x.y; hi[4 * c + 2] = x.z; hi[4 * c + 3] = x.w;
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < BK; ++k) hi[k] = *reinterpret_cast<const float*>(raw + 512 * k + 4 * r);
+        }
+#pragma unroll
+        for (int k = 0; k < BK; ++k) {
+          const float x = hi[k];
+          hi[k] = tc::tf32_rn_int(x);
+          lo[k] = tc::tf32_rn_int(x - hi[k]);
+        }
+        const uint32_t ta = tmem + ((uint32_t)(32 * warp) << 16) + TM_A + ps * 2 * BK;
+        tc::tmem_st32(ta, hi);
+        tc::tmem_st32(ta + BK, lo);
+      } else {
+#pragma unroll
+        for (int rep = 0; rep < 2; ++rep) {
+          const int idx = (tid - 128) + 128 * rep, sq = idx & 7, sg = idx >> 3;
+          const int jb = 8 * (sg & 3) + sq, kc = (sq + (sg >> 2)) & 7;
+          float v[4][4];
+          read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, jb, kc, v);
+          if constexpr (Pb::TILE_SCALE)
+            Pb::fixB_scaled(a, n0 + 4 * jb, k0 + 4 * kc, tscale + 4 * jb, v);
+          else
+            Pb::fixB(a, b, n0 + 4 * jb, k0 + 4 * kc, v);
+          tc::put4x4(pl + PB, pl + PB + PLANE, 4 * jb, kc, v);
+        }
+      }
       tc::fence_async_smem();   // generic-proxy plane writes -> visible to the MMAs
-      tc::tc_fence_before();    // orders this thread's earlier tcgen05.ld (drain) too
+      tc::tc_fence_before();    // orders the tcgen05.st of A and any earlier tcgen05.ld
       asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc::smem_u32(&pfull[ps]))
                    : "memory");
       QRB_GT(0, 3);
@@ -284,19 +343,20 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   tc::tc_fence_before();
   __syncthreads();
   QRB_GT(0, 6);
-  if (warp == 0) tc::tmem_dealloc(tmem, BN);
+  if (warp == 0) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
 // ---- policies: the tc_ops ones plus the raw-layout flags ----
 struct GramX : tc::GramTC {
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // X[k][m], X[k][j]
+  static constexpr bool A_TMEM = true;
   static constexpr bool TILE_SCALE = false;
-  __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 struct QApplyX : tc::QApplyTC {
   static constexpr bool A_KMAJOR = true, B_KMAJOR = true;    // X[m][k], RL[j][k]
+  // the R^{-1} transform makes B the heavier split: all threads share it (measured faster)
+  static constexpr bool A_TMEM = false;
   static constexpr bool TILE_SCALE = true;
-  __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
   __device__ static float col_scale(const Args& a, int64_t b, int j) {
     return (j < a.n) ? 1.f / sqrtf(a.D[b * a.n + j]) : 0.f;
   }
@@ -320,8 +380,8 @@ struct QApplyX : tc::QApplyTC {
 };
 struct ClosureX : tc::ClosureTC<float> {
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // Q[k][m], A[k][j]
+  static constexpr bool A_TMEM = true;
   static constexpr bool TILE_SCALE = false;
-  __device__ static void fixA(const Args&, int64_t, int, int, float (&)[4][4]) {}
 };
 
 }  // namespace tcx

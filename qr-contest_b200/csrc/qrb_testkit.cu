@@ -25,12 +25,12 @@ template <class Pb>
 static int tcx_launch(const void* a, bool ak, const void* b, bool bk, int n, int64_t batch,
                       const typename Pb::Args& args, cudaStream_t s) {
   tcx::Maps mp;
-  if (!encode_batched(&mp.a, a, n, batch, ak ? 128 : 32) ||
-      !encode_batched(&mp.b, b, n, batch, bk ? 128 : 32))
+  if (!(ak ? encode_batched(&mp.a, a, n, batch, 128) : encode_batched_wide(&mp.a, a, n, batch)) ||
+      !(bk ? encode_batched(&mp.b, b, n, batch, 128) : encode_batched_wide(&mp.b, b, n, batch)))
     return 999;
   cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       tcx::SMEM_BYTES);
-  tcx::tcx_gemm_kernel<Pb><<<g128(n, n, batch), tcx::XTHREADS, tcx::SMEM_BYTES, s>>>(mp, args);
+                       tcx::smem_bytes<Pb>());
+  tcx::tcx_gemm_kernel<Pb><<<g128(n, n, batch), tcx::XTHREADS, tcx::smem_bytes<Pb>(), s>>>(mp, args);
   return 0;
 }
 

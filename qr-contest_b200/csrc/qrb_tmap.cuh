@@ -42,4 +42,18 @@ inline bool encode_batched(CUtensorMap* map, const void* base, int n, int64_t ba
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Map over `batch` row-major n x n float32 matrices read as k-major operand tiles: box
+// {128 columns, 32 rows}, no swizzle (512-byte rows in shared memory), zero fill out of range.
+inline bool encode_batched_wide(CUtensorMap* map, const void* base, int n, int64_t batch) {
+  EncodeTiledFn fn = encode_tiled_fn();
+  if (!fn || (n & 3) || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  const cuuint64_t dims[3] = {(cuuint64_t)n, (cuuint64_t)n, (cuuint64_t)batch};
+  const cuuint64_t strides[2] = {(cuuint64_t)n * 4, (cuuint64_t)n * n * 4};
+  const cuuint32_t box[3] = {128, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 }  // namespace qrb
