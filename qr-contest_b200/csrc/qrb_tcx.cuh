@@ -120,6 +120,11 @@ __device__ __forceinline__ void read_raw(const char* raw, int rb, int kc, float 
 //   pfull[ps]   split -> issuer   planes of stage t written            (256 arrivals)
 //   mma_bar[ps] MMAs -> split     planes of stage t free / TMEM ready  (tcgen05.commit)
 constexpr int XTHREADS = NTHREADS + 32;
+#ifndef QRB_TCX_BALL
+#define QRB_TCX_BALL 1
+#endif
+// A-in-TMEM tiles: every split warp also takes one B micro-block (else warps 4-7 take two each)
+constexpr bool kBAll = QRB_TCX_BALL != 0;
 constexpr int TM_A = BN;              // TMEM: accumulator in columns [0, BN), A sets after it
 constexpr int TM_COLS = 256;          // BN + 2 sets x (hi, lo) x BK columns, power of two
 
@@ -167,7 +172,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   // per-column scale of the B transform (QApplyX: d_j^{-1/2}), read once per tile
-  __shared__ float tscale[BN];
+  __shared__ __align__(16) float tscale[BN];
   if constexpr (Pb::TILE_SCALE)
     for (int j = tid; j < BN; j += XTHREADS) tscale[j] = Pb::col_scale(a, b, n0 + j);
   tc::tc_fence_before();
@@ -282,10 +287,12 @@ __global__ void __launch_bounds__(XTHREADS, 1)
         const uint32_t ta = tmem + ((uint32_t)(32 * warp) << 16) + TM_A + ps * 2 * BK;
         tc::tmem_st32(ta, hi);
         tc::tmem_st32(ta + BK, lo);
-      } else {
+      }
+      if (Pb::A_TMEM && (kBAll || !a_role)) {
+        // B micro-blocks: one per thread over all 8 warps (kBAll), or two per thread of warps 4-7
 #pragma unroll
-        for (int rep = 0; rep < 2; ++rep) {
-          const int idx = (tid - 128) + 128 * rep, sq = idx & 7, sg = idx >> 3;
+        for (int rep = 0; rep < (kBAll ? 1 : 2); ++rep) {
+          const int idx = kBAll ? tid : (tid - 128) + 128 * rep, sq = idx & 7, sg = idx >> 3;
           const int jb = 8 * (sg & 3) + sq, kc = (sq + (sg >> 2)) & 7;
           float v[4][4];
           read_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, jb, kc, v);
@@ -354,8 +361,9 @@ struct GramX : tc::GramTC {
 };
 struct QApplyX : tc::QApplyTC {
   static constexpr bool A_KMAJOR = true, B_KMAJOR = true;    // X[m][k], RL[j][k]
-  // the R^{-1} transform makes B the heavier split: all threads share it (measured faster)
-  static constexpr bool A_TMEM = false;
+  // A (X rows) in TMEM; the transformed B is split by all 8 warps (1.35 / 1.84 ms per pass-1 /
+  // pass-2 launch of 768 matrices vs 1.41 / 1.96 with both operands in shared-memory planes)
+  static constexpr bool A_TMEM = true;
   static constexpr bool TILE_SCALE = true;
   __device__ static float col_scale(const Args& a, int64_t b, int j) {
     return (j < a.n) ? 1.f / sqrtf(a.D[b * a.n + j]) : 0.f;
@@ -364,6 +372,8 @@ struct QApplyX : tc::QApplyTC {
   __device__ static void fixB_scaled(const Args& a, int j0, int k0, const float* rs,
                                      float (&v)[4][4]) {
 #pragma unroll
+    const float4 r4 = *reinterpret_cast<const float4*>(rs);  // one 16-byte shared load
+    const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
     for (int i = 0; i < 4; ++i) {
       const int j = j0 + i;
 #pragma unroll
@@ -371,8 +381,8 @@ struct QApplyX : tc::QApplyTC {
         const int k = k0 + kk;
         float r;
         if (j >= a.n || k > j) r = 0.f;
-        else if (k < j) r = a.pass2 ? -(v[i][kk] * rs[i]) : v[i][kk] * rs[i];
-        else r = a.pass2 ? (1.f - rs[i]) : rs[i];
+        else if (k < j) r = a.pass2 ? -(v[i][kk] * rv[i]) : v[i][kk] * rv[i];
+        else r = a.pass2 ? (1.f - rv[i]) : rv[i];
         v[i][kk] = r;
       }
     }
