@@ -273,6 +273,8 @@ static cudaError_t set_common_attrs() {
   if ((e = small_attr<__nv_bfloat16>()) != cudaSuccess) return e;
   if ((e = small_attr<__half>()) != cudaSuccess) return e;
   if ((e = tcx_attr<tcx::GramX>()) != cudaSuccess) return e;
+  if ((e = tcx_attr<tcx::SyrkX>()) != cudaSuccess) return e;
+  if ((e = tcx_attr<tcx::LinvBlkX>()) != cudaSuccess) return e;
   if ((e = tcx_attr<tcx::QApplyX>()) != cudaSuccess) return e;
   return tcx_attr<tcx::ClosureX>();
 }
@@ -370,14 +372,24 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
                      LinvTrailArgs{n, k0, k1, nb, ws.R, ws.W, ws.Bp}));
     }
     if (ke < n) {
+      // TMA-fed tiles when the maps encode (16-byte aligned buffers), else the register-fed ones
+      const uint64_t un = (uint64_t)n, ul = (uint64_t)ldw;
+      tcx::Maps sm_, lm_;
+      const bool sx = encode_batched_wide(&sm_.a, ws.R, n, cb) && encode_batched_wide(&sm_.b, ws.R, n, cb);
+      const bool lx = encode_3d(&lm_.a, ws.W, ul, un, cb, ul * 4, un * ul * 4, 32, 128) &&
+                      encode_3d(&lm_.b, ws.Bp, un, ul, cb, un * 4, ul * un * 4, 128, 32);
+      const tc::SyrkTCArgs sa{n, kb, ke, ws.T0, ws.R, info};
+      const tc::LinvBlkArgs la{n, kb, ke, ldw, ws.R, ws.W, ws.Bp, info};
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 tc::tc_gemm_kernel<tc::SyrkTC, kTcBN><<<tc_grid(n - ke, n - ke, cb), tc::NTHREADS,
-                                                         kTcSmem, st>>>(
-                     tc::SyrkTCArgs{n, kb, ke, ws.T0, ws.R, info}));
+                 if (sx) tcx::tcx_gemm_kernel<tcx::SyrkX><<<tc_grid(n - ke, n - ke, cb), tcx::XTHREADS,
+                                                             tcx::smem_bytes<tcx::SyrkX>(), st>>>(sm_, sa);
+                 else tc::tc_gemm_kernel<tc::SyrkTC, kTcBN><<<tc_grid(n - ke, n - ke, cb), tc::NTHREADS,
+                                                              kTcSmem, st>>>(sa));
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 tc::tc_gemm_kernel<tc::LinvBlkTC, kTcBN><<<tc_grid(n - ke, ke, cb), tc::NTHREADS,
-                                                           kTcSmem, st>>>(
-                     tc::LinvBlkArgs{n, kb, ke, ldw, ws.R, ws.W, ws.Bp, info}));
+                 if (lx) tcx::tcx_gemm_kernel<tcx::LinvBlkX><<<tc_grid(n - ke, ke, cb), tcx::XTHREADS,
+                                                                tcx::smem_bytes<tcx::LinvBlkX>(), st>>>(lm_, la);
+                 else tc::tc_gemm_kernel<tc::LinvBlkTC, kTcBN><<<tc_grid(n - ke, ke, cb), tc::NTHREADS,
+                                                                kTcSmem, st>>>(la));
     }
   }
   const QApplyArgs qa{n, pass2 ? 1 : 0, X, ws.R, ws.D, Q, info};

@@ -193,11 +193,13 @@ __global__ void __launch_bounds__(XTHREADS, 1)
 
   if (issuer_warp) {
     if (lane == 0) {
+      int o_ar, o_ak, o_br, o_bk;  // where the operands start inside the mapped buffers
+      Pb::org(a, o_ar, o_ak, o_br, o_bk);
       auto issue = [&](int t) {  // raw tiles of k-step t into slot t % RAW_STAGES
         const int s = t % RAW_STAGES, k0 = kb + t * BK;
         mbar_expect_tx(&full[s], RAW_A + RAW_B);
-        issue_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, &maps.a, m0, k0, (int)b, &full[s]);
-        issue_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, &maps.b, n0, k0, (int)b, &full[s]);
+        issue_raw<Pb::A_KMAJOR>(rawA + s * RAW_A, &maps.a, m0 + o_ar, k0 + o_ak, (int)b, &full[s]);
+        issue_raw<Pb::B_KMAJOR>(rawB + s * RAW_B, &maps.b, n0 + o_br, k0 + o_bk, (int)b, &full[s]);
       };
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
@@ -357,6 +359,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
 struct GramX : tc::GramTC {
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // X[k][m], X[k][j]
   static constexpr bool A_TMEM = true;
+  __device__ static void org(const Args&, int& ar, int& ak, int& br, int& bk) { ar = ak = br = bk = 0; }
   static constexpr bool TILE_SCALE = false;
 };
 struct QApplyX : tc::QApplyTC {
@@ -364,6 +367,7 @@ struct QApplyX : tc::QApplyTC {
   // A (X rows) in TMEM; the transformed B is split by all 8 warps (1.35 / 1.84 ms per pass-1 /
   // pass-2 launch of 768 matrices vs 1.41 / 1.96 with both operands in shared-memory planes)
   static constexpr bool A_TMEM = true;
+  __device__ static void org(const Args&, int& ar, int& ak, int& br, int& bk) { ar = ak = br = bk = 0; }
   static constexpr bool TILE_SCALE = true;
   __device__ static float col_scale(const Args& a, int64_t b, int j) {
     return (j < a.n) ? 1.f / sqrtf(a.D[b * a.n + j]) : 0.f;
@@ -391,7 +395,34 @@ struct QApplyX : tc::QApplyTC {
 struct ClosureX : tc::ClosureTC<float> {
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // Q[k][m], A[k][j]
   static constexpr bool A_TMEM = true;
+  __device__ static void org(const Args&, int& ar, int& ak, int& br, int& bk) { ar = ak = br = bk = 0; }
   static constexpr bool TILE_SCALE = false;
+};
+
+// K = block updates of the two-level Cholesky elimination (see SyrkTC / LinvBlkTC in
+// qrb_tc_ops.cuh) on the TMA-fed tile.  org() places the operand tiles inside the mapped
+// buffers: SyrkX reads R rows [kb, ke) at columns [ke, n) for both operands (m-major);
+// LinvBlkX reads the W buffer (rows [ke, n), k-major, ldw columns) and the Bp buffer (ldw
+// rows of n columns, m-major).
+struct SyrkX : tc::SyrkTC {
+  static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // R[kb + k][ke + m]
+  static constexpr bool A_TMEM = true, TILE_SCALE = false;
+  __device__ static void org(const Args& a, int& ar, int& ak, int& br, int& bk) {
+    ar = br = a.k1;
+    ak = bk = a.k0;
+  }
+  __device__ static float row_scale(const Args&, int64_t, int) { return 0.f; }
+  __device__ static void fixA_row(const Args&, int, int, float, float (&)[BK]) {}
+};
+struct LinvBlkX : tc::LinvBlkTC {
+  static constexpr bool A_KMAJOR = true, B_KMAJOR = false;   // W[ke + m][k], Bp[k][j]
+  static constexpr bool A_TMEM = true, TILE_SCALE = false;
+  __device__ static void org(const Args& a, int& ar, int& ak, int& br, int& bk) {
+    ar = a.ke;
+    ak = br = bk = 0;
+  }
+  __device__ static float row_scale(const Args&, int64_t, int) { return 0.f; }
+  __device__ static void fixA_row(const Args&, int, int, float, float (&)[BK]) {}
 };
 
 }  // namespace tcx
