@@ -88,7 +88,10 @@ struct Prof {
 constexpr int kMaxN = 4096;
 constexpr int kSmallMax = 128;   // largest order the fused one-CTA-per-matrix kernel supports
 static std::atomic<int> g_small_n{64};  // n <= g_small_n: fused kernel, no workspace
-constexpr size_t kChunkBudget = size_t(8) << 30;  // float32 working set per chunk
+#ifndef QRB_CHUNK_GIB
+#define QRB_CHUNK_GIB 24
+#endif
+constexpr size_t kChunkBudget = size_t(QRB_CHUNK_GIB) << 30;  // float32 working set per chunk
 constexpr int64_t kMaxChunk = 65535;              // grid.y / grid.z limit
 constexpr size_t kPanelSmemCap = 200 * 1024;
 // column block of the two-level Cholesky elimination (QRB200_OPT_CHOL_BLOCK; 0 = one level)
