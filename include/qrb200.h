@@ -109,6 +109,11 @@ long long qrb200_launch_count(void);
  *   split over; they fork from and join back to the caller's stream, so the call keeps its
  *   stream semantics.  1 = everything on the caller's stream. */
 #define QRB200_OPT_LANES 4
+/*   QRB200_OPT_CHART_BLOCK: column block of the two-level chart elimination (0 = one level;
+ *   64, 128 (default) or 256): its 32-wide panels update only the block's columns and rows,
+ *   the rest of the trailing matrix takes one float32 K = block update per block.  Used when
+ *   n % 4 == 0 and n > block.  qrb200_workspace_bytes reflects the value set when it is called. */
+#define QRB200_OPT_CHART_BLOCK 5
 int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return

@@ -109,10 +109,15 @@ constexpr size_t kLaneSlack = 4 * 13 * 256;
 
 // Columns of the W / Wc panel buffers (rows of Bp): the panels of one Cholesky column block
 // keep theirs side by side when the two-level elimination runs (nb = 32, n > kCholBlock).
+static std::atomic<int> g_chart_block{128};  // QRB200_OPT_CHART_BLOCK (0 = one level)
 static int ws_cols(int n) {
   const int nb = pick_nb(n);
+  int c = nb;
   const int cb = g_chol_block.load(std::memory_order_relaxed);
-  return (nb == 32 && cb > 0 && n > cb) ? cb : nb;
+  const int hb = g_chart_block.load(std::memory_order_relaxed);
+  if (nb == 32 && cb > 0 && n > cb && cb > c) c = cb;
+  if (nb == 32 && hb > 0 && n > hb && hb > c) c = hb;
+  return c;
 }
 
 struct Ws {
@@ -479,23 +484,60 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   cholqr_pass(ws.Q1, ws.L, n, cb, nb, ws, info, INFO_CHOL2_NOT_PD, st, prof);
 
   // ---- III: chart on a copy of Q (working copy in ws.T0) ----
-  for (int k0 = 0; k0 < n; k0 += nb) {
-    const int w = (n - k0 < nb) ? n - k0 : nb;
-    const float* cur = (k0 == 0) ? ws.L : ws.T0;
-    PanelArgs pa{};
-    pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
-    pa.src = cur; pa.W = ws.W; pa.H = H; pa.tau = tau; pa.s = ws.s; pa.info = info;
-    QRB_LAUNCH(prof, F_CHART_PANEL,
-               (launch_panel<PM_CHART, float, T>(pa, cb, st)));
-    const int k1 = k0 + w;
-    // The chart stays on float32 FMA tiles: tau_k = 2/(1+|y_k|^2) sits at 1 when d_k = 0,
-    // and the 2^-21 products of 3xTF32 would push it below the tau >= 1 - 1e-6 gate.
-    if (k1 < n)
-      QRB_LAUNCH(prof, F_CHART_TRAIL,
-                 if (rw) rankw_kernel<RWTrail<float>><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
-                     RWTrailArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr, info});
-                 else simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
-                     TrailWArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr}));
+  // The chart's trailing updates stay on float32 FMA tiles: tau_k = 2/(1+|y_k|^2) sits at 1
+  // when d_k = 0, and the 2^-21 products of 3xTF32 would push it below the tau >= 1 - 1e-6 gate.
+  const int hblk = g_chart_block.load(std::memory_order_relaxed);
+  if (rw && nb == 32 && hblk > 0 && n > hblk) {
+    // Two-level: the 32-wide panels of a column block [kb, ke) update the block's columns for
+    // every row below and the block's rows for the columns right of it; the rest takes one
+    // K = ke - kb update per block (the panels' W column groups side by side, ldw = hblk).
+    // Everything runs in place on a copy of the frame.
+    e = cudaMemcpyAsync(ws.T0, ws.L, (size_t)cb * n * n * sizeof(float), cudaMemcpyDeviceToDevice, st);
+    if (e != cudaSuccess) return e;
+    for (int kb = 0; kb < n; kb += hblk) {
+      const int ke = (n - kb < hblk) ? n : kb + hblk;
+      for (int k0 = kb; k0 < ke; k0 += nb) {
+        const int w = (n - k0 < nb) ? n - k0 : nb;
+        const int k1 = k0 + w;
+        float* Wp = ws.W + (k0 - kb);
+        PanelArgs pa{};
+        pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = hblk;
+        pa.src = ws.T0; pa.W = Wp; pa.H = H; pa.tau = tau; pa.s = ws.s; pa.info = info;
+        QRB_LAUNCH(prof, F_CHART_PANEL, (launch_panel<PM_CHART, float, T>(pa, cb, st)));
+        if (k1 < ke) {
+          const RWGenArgs col{n, k1, k1, n - k1, ke - k1, w, k0, hblk, ws.T0, Wp, info};
+          QRB_LAUNCH(prof, F_CHART_TRAIL,
+                     rankw_kernel<RWGen><<<rw_grid(n - k1, ke - k1, cb), 256, 0, st>>>(col));
+          if (ke < n) {
+            const RWGenArgs row{n, k1, ke, ke - k1, n - ke, w, k0, hblk, ws.T0, Wp, info};
+            QRB_LAUNCH(prof, F_CHART_TRAIL,
+                       rankw_kernel<RWGen><<<rw_grid(ke - k1, n - ke, cb), 256, 0, st>>>(row));
+          }
+        }
+      }
+      if (ke < n) {
+        const RWGenArgs blk{n, ke, ke, n - ke, n - ke, ke - kb, kb, hblk, ws.T0, ws.W, info};
+        QRB_LAUNCH(prof, F_CHART_TRAIL,
+                   rankw_kernel<RWGen><<<rw_grid(n - ke, n - ke, cb), 256, 0, st>>>(blk));
+      }
+    }
+  } else {
+    for (int k0 = 0; k0 < n; k0 += nb) {
+      const int w = (n - k0 < nb) ? n - k0 : nb;
+      const float* cur = (k0 == 0) ? ws.L : ws.T0;
+      PanelArgs pa{};
+      pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
+      pa.src = cur; pa.W = ws.W; pa.H = H; pa.tau = tau; pa.s = ws.s; pa.info = info;
+      QRB_LAUNCH(prof, F_CHART_PANEL,
+                 (launch_panel<PM_CHART, float, T>(pa, cb, st)));
+      const int k1 = k0 + w;
+      if (k1 < n)
+        QRB_LAUNCH(prof, F_CHART_TRAIL,
+                   if (rw) rankw_kernel<RWTrail<float>><<<rw_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                       RWTrailArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr, info});
+                   else simt_gemm_kernel<TrailW<float>><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
+                       TrailWArgs{n, k0, k1, nb, cur, ws.T0, ws.W, nullptr}));
+    }
   }
   // ---- II: closure, H_upper = s * triu(Q^T A) ----
   tcx::Maps cm;
@@ -696,6 +738,11 @@ int qrb200_set_option(int32_t key, int64_t value) {
   if (key == QRB200_OPT_LANES) {
     if (value < 1 || value > qrb::kMaxLanes) return QRB200_ERR_INVALID_ARG;
     qrb::g_lanes.store((int)value);
+    return QRB200_OK;
+  }
+  if (key == QRB200_OPT_CHART_BLOCK) {
+    if (value != 0 && value != 64 && value != 128 && value != 256) return QRB200_ERR_INVALID_ARG;
+    qrb::g_chart_block.store((int)value);
     return QRB200_OK;
   }
   if (key == QRB200_OPT_CHOL_BLOCK) {

@@ -49,43 +49,48 @@ __global__ void __launch_bounds__(256) rankw_kernel(typename Pb::Args a) {
   if (m0 >= M || n0 >= N || !Pb::live(a, m0, n0)) return;
   const int tid = threadIdx.x;
 
-  // A: 64 rows x K (<= 32) -> As[k][m]
-#pragma unroll
-  for (int rep = 0; rep < 2; ++rep) {
-    const int mm = (tid >> 3) + 32 * rep, kc = tid & 7;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (m0 + mm < M && 4 * kc < K) v = __ldg(reinterpret_cast<const float4*>(Pb::a_ptr(a, b, m0 + mm) + 4 * kc));
-    As[4 * kc + 0][mm] = v.x;
-    As[4 * kc + 1][mm] = v.y;
-    As[4 * kc + 2][mm] = v.z;
-    As[4 * kc + 3][mm] = v.w;
-  }
-  // B: K rows x 128 columns -> Bs[k][j]
-#pragma unroll
-  for (int rep = 0; rep < 4; ++rep) {
-    const int k = (tid >> 5) + 8 * rep, c4 = (tid & 31) * 4;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (k < K && n0 + c4 < N) v = ld4v(Pb::b_ptr(a, b, k) + n0 + c4);
-    st4(&Bs[k][c4], v);
-  }
-  __syncthreads();
-
   const int tn = tid & 15, tm = tid >> 4;
   float acc[4][8];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
-  for (int k = 0; k < K; ++k) {
-    const float4 av = *reinterpret_cast<const float4*>(&As[k][tm * 4]);
-    const float4 b0 = *reinterpret_cast<const float4*>(&Bs[k][tn * 8]);
-    const float4 b1 = *reinterpret_cast<const float4*>(&Bs[k][tn * 8 + 4]);
-    const float ar[4] = {av.x, av.y, av.z, av.w};
-    const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+  // K is consumed in slices of RW_K = 32 (a single slice for the rank-32 panel updates)
+  for (int kb = 0; kb < K; kb += RW_K) {
+    const int Kc = (K - kb < RW_K) ? K - kb : RW_K;
+    if (kb > 0) __syncthreads();  // the previous slice has been read
+    // A: 64 rows x Kc -> As[k][m]
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int rep = 0; rep < 2; ++rep) {
+      const int mm = (tid >> 3) + 32 * rep, kc = tid & 7;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m0 + mm < M && 4 * kc < Kc)
+        v = __ldg(reinterpret_cast<const float4*>(Pb::a_ptr(a, b, m0 + mm) + kb + 4 * kc));
+      As[4 * kc + 0][mm] = v.x;
+      As[4 * kc + 1][mm] = v.y;
+      As[4 * kc + 2][mm] = v.z;
+      As[4 * kc + 3][mm] = v.w;
+    }
+    // B: Kc rows x 128 columns -> Bs[k][j]
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+    for (int rep = 0; rep < 4; ++rep) {
+      const int k = (tid >> 5) + 8 * rep, c4 = (tid & 31) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < Kc && n0 + c4 < N) v = ld4v(Pb::b_ptr(a, b, kb + k) + n0 + c4);
+      st4(&Bs[k][c4], v);
+    }
+    __syncthreads();
+    for (int k = 0; k < Kc; ++k) {
+      const float4 av = *reinterpret_cast<const float4*>(&As[k][tm * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[k][tn * 8]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[k][tn * 8 + 4]);
+      const float ar[4] = {av.x, av.y, av.z, av.w};
+      const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+    }
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -225,6 +230,40 @@ struct RWLinv {
     } else {
       st4(p, x);
     }
+  }
+};
+
+// ---- general in-place rank-K update of a block of each matrix (K may exceed 32) ----------
+//   C[r0 + m][c0 + j] -= sum_k W[r0 + m][k] * C[kb + k][c0 + j],  m < M, j < N, k < K
+// W rows have ldw columns (the pointer already at the first column used).  The B rows
+// [kb, kb + K) must not overlap the updated rows [r0, r0 + M) (they are read while others
+// are written).  Used by the two-level chart elimination.
+struct RWGenArgs {
+  int n, r0, c0, M, N, K, kb, ldw;
+  float* C;
+  const float* W;
+  int* info;
+};
+struct RWGen {
+  using Args = RWGenArgs;
+  __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
+  __device__ static void dims(const Args& a, int& M, int& N, int& K) {
+    M = a.M;
+    N = a.N;
+    K = a.K;
+  }
+  __device__ static bool live(const Args&, int, int) { return true; }
+  __device__ static const float* a_ptr(const Args& a, int64_t b, int m) {
+    return a.W + ((int64_t)b * a.n + a.r0 + m) * a.ldw;
+  }
+  __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
+    return a.C + mat_off(b, a.n) + (int64_t)(a.kb + k) * a.n + a.c0;
+  }
+  __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
+    return ld4rw(a.C + mat_off(b, a.n) + (int64_t)(a.r0 + m) * a.n + a.c0 + j);
+  }
+  __device__ static void store4(const Args& a, int64_t b, int m, int j, float4 x) {
+    st4(a.C + mat_off(b, a.n) + (int64_t)(a.r0 + m) * a.n + a.c0 + j, x);
   }
 };
 

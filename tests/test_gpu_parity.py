@@ -266,3 +266,21 @@ def test_lanes_bit_identical(lanes):
         _lib.set_lanes(2)
     assert torch.equal(H, H0) and torch.equal(Hc, H0)
     assert torch.equal(tau, t0) and torch.equal(info, i0)
+
+
+@pytest.mark.parametrize("block", [0, 64, 256])
+@pytest.mark.parametrize("n", [192, 320, 512])
+def test_chart_block_widths(block, n):
+    """The two-level chart elimination at every block width (0 = one level) against the
+    default width on the same inputs: gates on all six classes, tight agreement on the
+    well-determined classes."""
+    from qrb200 import _lib, generators as G
+    A = G.heterogeneous(12, n, seed=47, device="cuda")
+    H0, t0 = run(A)
+    _lib.set_chart_block(block)
+    try:
+        H, tau = run(A)
+    finally:
+        _lib.set_chart_block(128)
+    assert_gates(A, H, tau, f"chart block={block} n={n}")
+    assert_tight(H[:2], tau[:2], H0[:2].cpu().numpy(), t0[:2].cpu().numpy())
