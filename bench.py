@@ -114,6 +114,30 @@ def family_bytes(n: int) -> dict:
         b["lu_trail"] += 4.0 * (2 * t * t + t * w + w * t)
         b["chart_trail"] += 4.0 * (2 * t * t + t * w + w * t)
         b["chol_trail"] += 2 * 4.0 * (t * t + 2 * t * w + 2 * t * k1)  # G lower half, L_G^-1
+    # two-level Cholesky and chart eliminations (the library's default block of 128 columns
+    # when 32-wide panels are used and n > 128): C moves once per panel only inside the block
+    # strips, and once per block for the rest
+    blk = 128
+    if nb == 32 and n > blk and n % 4 == 0:
+        chol = chart = 8.0 * n * n  # chart: the frame copied into the working buffer once
+        for kb in range(0, n, blk):
+            ke = min(n, kb + blk)
+            for k0 in range(kb, ke, nb):
+                w = min(nb, n - k0)
+                k1 = k0 + w
+                c = ke - k1
+                # Cholesky: block columns of every row below (lower part), L_G^-1 rows in block
+                chol += 8.0 * ((n - k1) * c - c * (c - 1) / 2) + 4.0 * ((n - k1) * w + w * c)
+                chol += 4.0 * ((ke - k1) * k0 + (ke - k0) * k1 + (ke - k0) * w + w * k1)
+                # chart: block columns of every row below, block rows right of the block
+                chart += 8.0 * ((n - k1) * c + c * (n - ke)) + 4.0 * ((n - k1) * w + w * (n - k1))
+            t2, K = n - ke, ke - kb
+            if t2 > 0:
+                chol += 8.0 * t2 * (t2 + 1) / 2 + 4.0 * 2 * K * t2           # trailing triangle
+                chol += 4.0 * (t2 * kb + t2 * ke + t2 * K + K * ke)          # L_G^-1 rows below
+                chart += 8.0 * t2 * t2 + 4.0 * 2 * K * t2
+        b["chol_trail"] = 2 * chol
+        b["chart_trail"] = chart
     b["gram"] = 2 * 4.0 * (n * n + n * n / 2)
     b["q_apply"] = 4.0 * (2 * n * n + n * n / 2) + 4.0 * (3 * n * n + n * n / 2)
     b["closure"] = 4.0 * (2 * n * n + n * n / 2)
