@@ -353,7 +353,14 @@ def run_qrb(args):
     else:
         roof = {"bound": "hbm", "achieved": fb / t_dom / 1e9, "peak": hbm, "unit": "GB/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
-    roof["traffic"] = None
+    # DRAM bytes per matrix of the chol_trail kernels from an ncu capture of the same
+    # configuration at 256 matrices (dram__bytes_read.sum + dram__bytes_write.sum summed over
+    # the family's launches), scaled to the batch; writes that were still in L2 when each
+    # profiled launch ended are not in it
+    traffic_per_matrix = {("chol_trail", 512): 9.54e6}.get((dom, n))
+    roof["traffic"] = traffic_per_matrix * B if traffic_per_matrix else None
+    if traffic_per_matrix:
+        roof["traffic_unit"] = "bytes per step (ncu, 256-matrix capture scaled to the batch)"
     roof["kernel"] = dom
     roof["peak_source"] = (f"{src} MEASURED_PEAKS.json: bf16 {bf16} TF/s / 2 (TF32) / 3 "
                            f"(3xTF32), HBM {hbm} GB/s")
