@@ -105,3 +105,29 @@ def test_small_n_option():
     finally:
         _lib.set_small_n(64)
     assert _lib.workspace_bytes(7, 64) == 0
+
+
+def test_block_and_lane_options():
+    """Option ranges are enforced on the host; the block widths size the panel buffers, so
+    the workspace query follows them (one-level eliminations need the least)."""
+    L = _lib.lib()
+    for key, bad in ((_lib.OPT_CHOL_BLOCK, (1, 32, 100, 512, -1)),
+                     (_lib.OPT_CHART_BLOCK, (1, 32, 100, 512, -1)),
+                     (_lib.OPT_LANES, (0, 5, -1))):
+        for v in bad:
+            assert L.qrb200_set_option(key, v) == _lib.QRB200_ERR_INVALID_ARG, (key, v)
+    try:
+        default = _lib.workspace_bytes(8, 512)
+        _lib.set_chol_block(0)
+        _lib.set_chart_block(0)
+        one_level = _lib.workspace_bytes(8, 512)
+        _lib.set_chol_block(256)
+        wide = _lib.workspace_bytes(8, 512)
+        assert one_level < default < wide
+        for lanes in (1, 2, 3, 4):
+            _lib.set_lanes(lanes)
+    finally:
+        _lib.set_chol_block(128)
+        _lib.set_chart_block(128)
+        _lib.set_lanes(2)
+    assert _lib.workspace_bytes(8, 512) == default
