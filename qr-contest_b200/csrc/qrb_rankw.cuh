@@ -1,4 +1,5 @@
-// qrb200 -- rank-w trailing updates (w <= 32) as one memory-streaming pass per panel.
+// qrb200 -- rank-w trailing updates as one memory-streaming pass per update (K = the panel
+// width 32, or K = 128 for the chart's block update: K is consumed in slices of 32).
 //
 // Every blocked elimination of the pipeline ends a panel with C' = C - A B where K = w is
 // the panel width: the LU and chart trailing updates (reflection_no_reflectors.py:66 via

@@ -1,16 +1,19 @@
 // qrb200 -- TMA-fed 3xTF32 tcgen05 GEMM tile for the float32 n^3 stages (Grams, R^{-1} apply,
-// float32 closure).
+// float32 closure) and the K = 128 block updates of the two-level Cholesky elimination.
 //
 // Same mathematics and policies as tc_gemm_kernel (qrb_tc.cuh / qrb_tc_ops.cuh), different
-// data movement: raw float32 tiles are brought into a shared-memory ring by
-// cp.async.bulk.tensor (3-deep ring, SWIZZLE_128B, completion counted on an mbarrier), so no
-// thread waits on global loads.  All 256 threads then split a raw tile into hi/lo tf32 planes
-// (two plane sets, so the split of stage t+1 overlaps the MMAs of stage t; K-major SW128,
-// the UMMA operand layout), transposing M-major tiles in registers; one elected thread issues
-// the 12 MMAs of the stage and commits to an mbarrier that frees the planes.  Raw tiles of an
-// operand stored M-major (A(m,k) = X[k][m]) arrive as four 32 x 32 boxes; K-major operands
-// (A(m,k) = X[m][k]) as one 128-row box.  Out-of-range boxes are zero-filled by the TMA unit.
-// No multicast: every CTA loads its own tiles (the library also runs on 2-8 GPUs).
+// data movement.  One 128 x 128 output tile per CTA, 9 warps:
+//  * one lane of warp 8 brings raw float32 tiles into a 3-deep shared-memory ring with
+//    cp.async.bulk.tensor (k-major operands: one {32 k, 128 row} SWIZZLE_128B box; m-major
+//    operands: one unswizzled {128 row, 32 k} box), then issues the 12 MMAs of each stage and
+//    commits them to an mbarrier;
+//  * warps 0-7 split the raw tiles into tf32 hi / lo parts: for A_TMEM policies warps 0-3 write
+//    A's rows straight into tensor memory (tcgen05.st; the MMA reads A from TMEM) and all 8
+//    warps split B into shared-memory planes (K-major SW128, the UMMA operand layout); other
+//    policies split both operands into planes.  Two plane / TMEM sets let the split of stage
+//    t+1 overlap the MMAs of stage t.  Hand-offs are mbarriers only (no CTA barrier per stage).
+// Out-of-range boxes are zero-filled by the TMA unit.  No multicast: every CTA loads its own
+// tiles (the library also runs on 2-8 GPUs).
 #pragma once
 #include <cuda.h>
 
