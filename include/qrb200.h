@@ -132,10 +132,13 @@ const char* qrb200_last_cuda_error(void);
  * batch is factored in chunks that fit it.  The function calls no cudaMalloc, cudaFree or
  * allocating library routine.
  *  - Same arguments, results and info bits as qrb200_geqrf_batched (no workspace).
- *  - Returns QRB200_ERR_SCRATCH_LIMIT when a single n x n problem does not fit the scratch
- *    (n above 1820 for the 64 MiB array).
- *  - The first call on each device (with that device current) looks up the array's device
- *    address; make it before any stream capture.
+ *  - Returns QRB200_ERR_SCRATCH_LIMIT, before it touches the buffers or the device, when the
+ *    working set of a single n x n problem does not fit the scratch: n above 1826 with the
+ *    default options (the bound moves with QRB200_OPT_CHOL_BLOCK / QRB200_OPT_CHART_BLOCK,
+ *    which size the panel buffers).
+ *  - The first call in each CUDA context of a device (with that device current) looks up the
+ *    array's device address; make it before any stream capture.  A device reset creates a
+ *    new context and the next call looks the address up again.
  *  - All calls share the array: calls that overlap on the GPU (other streams or threads)
  *    race and must be serialized by the caller. */
 int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, int32_t* info,

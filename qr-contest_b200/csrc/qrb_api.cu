@@ -287,17 +287,56 @@ static cudaError_t set_common_attrs() {
   return tcx_attr<tcx::ClosureX>();
 }
 
-static cudaError_t ensure_attrs() {
-  static std::mutex mu;
-  static bool done[128] = {false};
+// Identity of the CUDA context current on this thread, making the device's primary context
+// current first when none is.  Per-device caches (kernel attributes, internal streams, the
+// allocation-free scratch address, the host-path staging buffers) are keyed on it as well as
+// on the device index: after cudaDeviceReset the primary context is created again, module
+// globals may move, and streams and allocations of the old context are gone.
+static cudaError_t current_ctx(int* dev_out, unsigned long long* id_out) {
+  using GetCur = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCur get_cur = nullptr;
+  static GetId get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_cur = reinterpret_cast<GetCur>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(p);
+  });
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  CUcontext c = nullptr;
+  if (!get_cur || get_cur(&c) != CUDA_SUCCESS) return cudaErrorNotSupported;
+  if (!c) {  // no context yet: cudaSetDevice initializes the primary context (CUDA 12+)
+    if ((e = cudaSetDevice(dev)) != cudaSuccess) return e;
+    if (get_cur(&c) != CUDA_SUCCESS || !c) return cudaErrorDeviceUninitialized;
+  }
+  unsigned long long id = 0;
+  if (!get_id || get_id(c, &id) != CUDA_SUCCESS) return cudaErrorNotSupported;
+  *dev_out = dev;
+  *id_out = id;
+  return cudaSuccess;
+}
+
+static cudaError_t ensure_attrs() {
+  static std::mutex mu;
+  static unsigned long long done_ctx[128] = {0};  // context whose attributes are set
+  int dev = 0;
+  unsigned long long ctx = 0;
+  cudaError_t e = current_ctx(&dev, &ctx);
+  if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> g(mu);
-  if (done[dev]) return cudaSuccess;
+  if (done_ctx[dev] == ctx) return cudaSuccess;
   e = set_common_attrs();
-  if (e == cudaSuccess) done[dev] = true;
+  if (e == cudaSuccess) done_ctx[dev] = ctx;
   return e;
 }
 
@@ -560,15 +599,16 @@ static std::atomic<int> g_lanes{2};  // QRB200_OPT_LANES
 static cudaStream_t* lane_streams() {
   static std::mutex mu;
   static cudaStream_t lanes[128][kMaxLanes];
-  static bool made[128] = {false};
+  static unsigned long long made_ctx[128] = {0};  // context the streams belong to
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return nullptr;
+  unsigned long long ctx = 0;
+  if (note(current_ctx(&dev, &ctx)) != cudaSuccess) return nullptr;
   std::lock_guard<std::mutex> g(mu);
-  if (!made[dev]) {
+  if (made_ctx[dev] != ctx) {  // streams of a context that was reset are gone with it
     for (int l = 0; l < kMaxLanes; ++l)
       if (note(cudaStreamCreateWithFlags(&lanes[dev][l], cudaStreamNonBlocking)) != cudaSuccess)
         return nullptr;
-    made[dev] = true;
+    made_ctx[dev] = ctx;
   }
   return lanes[dev];
 }
@@ -793,19 +833,23 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratch
 
 static std::mutex g_noalloc_mu;
 static void* g_noalloc_ptr[128] = {nullptr};
+static unsigned long long g_noalloc_ctx[128] = {0};
 
-// Device address of g_noalloc_scratch on the current device (looked up once per device).
+// Device address of g_noalloc_scratch in the current context: looked up on the first call in
+// each context of each device (a reset device gets a new context, where the array may sit
+// elsewhere) and cached.
 static cudaError_t noalloc_scratch(void** out) {
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  unsigned long long ctx = 0;
+  cudaError_t e = current_ctx(&dev, &ctx);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
   std::lock_guard<std::mutex> g(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  if (!g_noalloc_ptr[dev] || g_noalloc_ctx[dev] != ctx) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess) return e;
     g_noalloc_ptr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *out = g_noalloc_ptr[dev];
   return cudaSuccess;
@@ -844,9 +888,12 @@ extern "C" int qrb200_geqrf_batched_noalloc(const void* A, void* H, void* tau, i
   if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
     return QRB200_ERR_INVALID_ARG;
   if (batch == 0 || n == 0) return QRB200_OK;
-  if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
-  const int64_t cb = qrb::noalloc_chunk(n, qrb::ws_cols(n));
+  // the size check comes first: it needs no device and no valid buffers
+  // (orders of the fused kernel use no scratch: one launch covers up to 2^30 matrices)
+  const int64_t cb = n <= qrb::g_small_n.load() ? (int64_t(1) << 30)
+                                                : qrb::noalloc_chunk(n, qrb::ws_cols(n));
   if (cb < 1) return QRB200_ERR_SCRATCH_LIMIT;
+  if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
   if (qrb::note(qrb::ensure_attrs()) != cudaSuccess) return QRB200_ERR_CUDA;
   void* scratch = nullptr;
   if (qrb::note(qrb::noalloc_scratch(&scratch)) != cudaSuccess) return QRB200_ERR_CUDA;
@@ -879,6 +926,7 @@ constexpr int kHostSlots = 3;
 struct HostStaging {
   void* base = nullptr;
   size_t bytes = 0;
+  unsigned long long ctx = 0;  // context the buffer was allocated in
 };
 static std::mutex g_host_mu;
 static HostStaging g_host_staging[128];
@@ -916,10 +964,11 @@ extern "C" int qrb200_geqrf_batched_host(const void* A, void* H, void* tau, int3
   const size_t slot_bytes = 2 * a_b + t_b + i_b + w_b;
 
   int dev = 0;
-  if (note(cudaGetDevice(&dev)) != cudaSuccess) return QRB200_ERR_CUDA;
-  if (dev < 0 || dev >= 128) return QRB200_ERR_CUDA;
+  unsigned long long ctx = 0;
+  if (note(current_ctx(&dev, &ctx)) != cudaSuccess) return QRB200_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_host_mu);
   HostStaging& hs = g_host_staging[dev];
+  if (hs.base && hs.ctx != ctx) hs = HostStaging{};  // freed with the context it came from
   const size_t need = kHostSlots * slot_bytes;
   if (hs.bytes < need) {
     if (hs.base && note(cudaFree(hs.base)) != cudaSuccess) return QRB200_ERR_CUDA;
@@ -927,6 +976,7 @@ extern "C" int qrb200_geqrf_batched_host(const void* A, void* H, void* tau, int3
     hs.bytes = 0;
     if (note(cudaMalloc(&hs.base, need)) != cudaSuccess) return QRB200_ERR_CUDA;
     hs.bytes = need;
+    hs.ctx = ctx;
   }
   cudaStream_t caller = static_cast<cudaStream_t>(stream);
   cudaStream_t st[kHostSlots] = {};
@@ -980,11 +1030,11 @@ extern "C" int qrb200_geqrf_batched_host(const void* A, void* H, void* tau, int3
 extern "C" int qrb200_release_host_staging(void) {
   using namespace qrb;
   int dev = 0;
-  if (note(cudaGetDevice(&dev)) != cudaSuccess) return QRB200_ERR_CUDA;
-  if (dev < 0 || dev >= 128) return QRB200_ERR_CUDA;
+  unsigned long long ctx = 0;
+  if (note(current_ctx(&dev, &ctx)) != cudaSuccess) return QRB200_ERR_CUDA;
   std::lock_guard<std::mutex> lock(g_host_mu);
   HostStaging& hs = g_host_staging[dev];
-  if (hs.base && note(cudaFree(hs.base)) != cudaSuccess) return QRB200_ERR_CUDA;
+  if (hs.base && hs.ctx == ctx && note(cudaFree(hs.base)) != cudaSuccess) return QRB200_ERR_CUDA;
   hs.base = nullptr;
   hs.bytes = 0;
   return QRB200_OK;

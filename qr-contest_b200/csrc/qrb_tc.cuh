@@ -13,7 +13,9 @@
 // gathers, transposed operands, bf16/f16 inputs), so only one descriptor form is needed.
 //
 // Every wait is bounded: on timeout the kernel raises INFO_DEVICE_TIMEOUT in the matrix's
-// info word, skips the rest of its work, and still frees its TMEM.
+// info word, stops issuing MMAs and copies, waits (again bounded) for the ones already in
+// flight, and frees its TMEM only when that drain completed (a tile whose drain also timed
+// out leaves its TMEM allocated rather than free it under a running MMA).
 #pragma once
 #include "qrb_common.cuh"
 
@@ -59,10 +61,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 // Bounded wait; returns false on timeout.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
-  for (unsigned i = 0; i < kSpinLimit; ++i)
+__device__ __forceinline__ bool mbar_wait_n(uint64_t* bar, uint32_t phase, unsigned limit) {
+  for (unsigned i = 0; i < limit; ++i)
     if (mbar_try_wait(bar, phase)) return true;
   return false;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
+  return mbar_wait_n(bar, phase, kSpinLimit);
 }
 
 // ---- TMEM ----
@@ -265,6 +270,7 @@ __global__ void __launch_bounds__(NTHREADS, BN == 64 ? 2 : 1) tc_gemm_kernel(typ
   constexpr uint32_t IDESC = idesc_tf32(BM, BN);
   const int nk = (ke > kb) ? (ke - kb + BK - 1) / BK : 0;
   bool ok = true;
+  int last = nk - 1;       // last iteration whose MMAs were issued and committed
   uint32_t phasebits = 0;  // bit s = parity of the next wait on bars[s]
 
   if (nk > 0) {
@@ -299,15 +305,19 @@ __global__ void __launch_bounds__(NTHREADS, BN == 64 ? 2 : 1) tc_gemm_kernel(typ
       }
       if (ok) put(s2, kb + (it + 1) * BK);
       if (it + 2 < nk) fetch(kb + (it + 2) * BK);
-      __syncthreads();
+      // a timeout anywhere stops the issue of further MMAs for the whole CTA
+      if (__syncthreads_or(!ok)) { ok = false; last = it; break; }
     }
   }
-  // commits are cumulative: the last one covers every MMA issued before it
-  if (nk >= 1) {
-    const int s = (nk - 1) & 1;
-    if (!mbar_wait(&bars[s], (phasebits >> s) & 1)) ok = false;
-    phasebits ^= 1u << s;
+  // Commits are cumulative: the last one covers every MMA issued before it.  Commit j
+  // completes phase j / 2 of bars[j % 2].  On the timeout path this is also the drain: the
+  // TMEM is freed below only when it completed.
+  bool drained = true;
+  if (last >= 0) {
+    if (!mbar_wait(&bars[last & 1], (last >> 1) & 1)) ok = drained = false;
   }
+  ok = !__syncthreads_or(!ok);
+  drained = __syncthreads_and(drained);
   tc_fence_after();
 
   // ---- epilogue: warp w reads TMEM lanes 32*(w%4) .. +31, column half w/4 ----
@@ -330,7 +340,7 @@ __global__ void __launch_bounds__(NTHREADS, BN == 64 ? 2 : 1) tc_gemm_kernel(typ
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, BN);
+  if (warp == 0 && drained) tmem_dealloc(tmem, BN);
 }
 
 }  // namespace tc

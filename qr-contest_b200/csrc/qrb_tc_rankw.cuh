@@ -91,7 +91,12 @@ __global__ void __launch_bounds__(NTHREADS, 3) tc_rankw_kernel(typename Pb::Args
     }
     mma_commit(bar);
   }
-  const bool ok = mbar_wait(bar, 0);
+  // one commit (phase 0); a thread whose wait timed out makes the whole CTA skip the
+  // epilogue, and thread 0 waits once more so that the TMEM is not freed under the MMAs
+  bool ok = !__syncthreads_or(!mbar_wait(bar, 0));
+  bool drained = true;
+  if (!ok && tid == 0) drained = mbar_wait(bar, 0);
+  drained = __syncthreads_and(drained);
   tc_fence_after();
   if (ok) {
     // TMEM -> shared staging (row = TMEM lane), the operand planes are free now
@@ -125,7 +130,7 @@ __global__ void __launch_bounds__(NTHREADS, 3) tc_rankw_kernel(typename Pb::Args
     }
   }
   __syncthreads();
-  if (warp == 0) tmem_dealloc(tmem, 128);
+  if (warp == 0 && drained) tmem_dealloc(tmem, 128);
 }
 
 }  // namespace tc

@@ -162,11 +162,16 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   long long gt_prev_ = clock64();
 #endif
 
+  // issuer-side progress (TMA stages issued, MMA stages committed) and whether a timeout's
+  // drain completed; read after the CTA barrier that follows the role loops
+  __shared__ int s_issued, s_committed, s_drained;
   if (warp == 0) {
     tc::tmem_alloc(tslot, TM_COLS);
     tc::tmem_relinquish();
   }
   if (tid == 0) {
+    s_issued = s_committed = 0;
+    s_drained = 1;
     for (int s = 0; s < RAW_STAGES; ++s) tc::mbar_init(&full[s], 1);
     for (int p = 0; p < PLANE_SETS; ++p) {
       tc::mbar_init(&mma_bar[p], 1);
@@ -206,15 +211,19 @@ __global__ void __launch_bounds__(XTHREADS, 1)
       };
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.a)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&maps.b)) : "memory");
-      for (int t = 0; t < nk && t < RAW_STAGES; ++t) issue(t);
+      for (int t = 0; t < nk && t < RAW_STAGES; ++t) { issue(t); s_issued = t + 1; }
       constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
       for (int t = 0; t < nk; ++t) {
         const int ps = t & 1;
         char* pl = pl0 + ps * PSET;
-        if (ok && !tc::mbar_wait(&pfull[ps], (t >> 1) & 1)) ok = false;
+        // on a timeout nothing more is issued; what is in flight is drained below
+        if (!tc::mbar_wait(&pfull[ps], (t >> 1) & 1)) { ok = false; break; }
         tc::tc_fence_after();
         QRB_GT(NTHREADS, 4);
-        if (t + RAW_STAGES < nk) issue(t + RAW_STAGES);  // slot t % RAW_STAGES has been split
+        if (t + RAW_STAGES < nk) {  // slot t % RAW_STAGES has been split
+          issue(t + RAW_STAGES);
+          s_issued = t + RAW_STAGES + 1;
+        }
         const uint32_t bh = tc::smem_u32(pl + PB), bl = tc::smem_u32(pl + PB + PLANE);
 #pragma unroll
         for (int kk = 0; kk < BK / UK; ++kk) {
@@ -235,6 +244,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
           }
         }
         tc::mma_commit(&mma_bar[ps]);
+        s_committed = t + 1;
         QRB_GT(NTHREADS, 5);
       }
     }
@@ -333,7 +343,20 @@ __global__ void __launch_bounds__(XTHREADS, 1)
     tc::tc_fence_after();
   }
 
-  if (__syncthreads_or(!ok)) {
+  const bool failed = __syncthreads_or(!ok);
+  if (failed && issuer_warp && lane == 0) {
+    // Drain before the TMEM is freed and the CTA exits: the last commit covers every MMA
+    // issued (commit t completes phase t / 2 of mma_bar[t % 2]), and each of the last
+    // RAW_STAGES TMA stages issued completes phase u / RAW_STAGES of full[u % RAW_STAGES]
+    // (parity waits do not consume a phase, so waiting on one already seen is harmless).
+    bool drained = true;
+    const int nc = s_committed, ni = s_issued;
+    if (nc > 0 && !tc::mbar_wait(&mma_bar[(nc - 1) & 1], ((nc - 1) >> 1) & 1)) drained = false;
+    for (int u = (ni > RAW_STAGES ? ni - RAW_STAGES : 0); u < ni; ++u)
+      if (!tc::mbar_wait(&full[u % RAW_STAGES], (u / RAW_STAGES) & 1)) drained = false;
+    if (!drained) s_drained = 0;
+  }
+  if (failed) {
     if (tid == 0) atomicOr(Pb::info(a, b), INFO_DEVICE_TIMEOUT);
   } else if (!issuer_warp) {
     const int m = m0 + 32 * lq + lane;
@@ -355,7 +378,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   tc::tc_fence_before();
   __syncthreads();
   QRB_GT(0, 6);
-  if (warp == 0) tc::tmem_dealloc(tmem, TM_COLS);
+  if (warp == 0 && s_drained) tc::tmem_dealloc(tmem, TM_COLS);
 }
 
 // ---- policies: the tc_ops ones plus the raw-layout flags ----
@@ -378,9 +401,9 @@ struct QApplyX : tc::QApplyTC {
   // QApplyTC::fixB with d_j^{-1/2} from the tile's shared copy (rs[i] for column j0 + i)
   __device__ static void fixB_scaled(const Args& a, int j0, int k0, const float* rs,
                                      float (&v)[4][4]) {
-#pragma unroll
     const float4 r4 = *reinterpret_cast<const float4*>(rs);  // one 16-byte shared load
     const float rv[4] = {r4.x, r4.y, r4.z, r4.w};
+#pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int j = j0 + i;
 #pragma unroll

@@ -218,3 +218,37 @@ extern "C" int qrbt_tcx_timing(const float* X, float* G, int* info, int64_t batc
   cudaMemcpyFromSymbol(cycles_out, g_panel_timers, 8 * sizeof(long long));
   return (int)cudaGetLastError();
 }
+
+// ---- bounded-wait failure path (no GPU fault involved) ----
+// Each CTA holds TMEM like the production tiles, then waits with a short limit on an
+// mbarrier that no thread arrives at and no copy or MMA targets, so the wait runs out.  The
+// CTA takes the production tiles' timeout path: INFO_DEVICE_TIMEOUT into its info word,
+// nothing in flight to drain, TMEM freed, normal return.  The host then checks the bits and
+// that the context still runs tensor-core work.
+__global__ void timeout_probe_kernel(int* info, unsigned limit) {
+  __shared__ uint64_t bar;
+  __shared__ uint32_t slot;
+  const int tid = threadIdx.x;
+  if (tid < 32) {
+    tc::tmem_alloc(&slot, 32);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    tc::mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const bool ok = !__syncthreads_or(!tc::mbar_wait_n(&bar, 0, limit));
+  if (!ok && tid == 0) atomicOr(&info[blockIdx.x], INFO_DEVICE_TIMEOUT);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (tid < 32) tc::tmem_dealloc(slot, 32);
+}
+
+extern "C" int qrbt_timeout_probe(int* info, int blocks, unsigned limit, void* st) {
+  if (blocks < 1 || limit < 1 || limit > (1u << 20)) return (int)cudaErrorInvalidValue;
+  timeout_probe_kernel<<<blocks, 128, 0, (cudaStream_t)st>>>(info, limit);
+  return (int)cudaGetLastError();
+}

@@ -18,6 +18,8 @@ QRB200_ERR_WORKSPACE = 3
 QRB200_ERR_CUDA = 4
 QRB200_ERR_SCRATCH_LIMIT = 5
 NOALLOC_SCRATCH_BYTES = 64 << 20
+# largest n the allocation-free entry point accepts with the default block options
+NOALLOC_MAX_N_DEFAULT = 1826
 
 QRB200_F32, QRB200_BF16, QRB200_F16 = 0, 1, 2
 

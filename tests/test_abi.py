@@ -131,3 +131,17 @@ def test_block_and_lane_options():
         _lib.set_chart_block(128)
         _lib.set_lanes(2)
     assert _lib.workspace_bytes(8, 512) == default
+
+
+def test_noalloc_order_limit_without_gpu():
+    # the allocation-free entry point checks the order against its built-in scratch before it
+    # looks at the buffers or the device: with null buffers an order that fits reports an
+    # invalid argument, one that does not fit reports the scratch limit
+    from qrb200 import _lib
+    L = _lib.lib()
+    nmax = _lib.NOALLOC_MAX_N_DEFAULT
+    call = lambda n: L.qrb200_geqrf_batched_noalloc(None, None, None, None, 1, n,  # noqa: E731
+                                                    _lib.QRB200_F32, None)
+    assert call(nmax) == _lib.QRB200_ERR_INVALID_ARG
+    assert call(nmax + 1) == _lib.QRB200_ERR_SCRATCH_LIMIT
+    assert call(64) == _lib.QRB200_ERR_INVALID_ARG

@@ -159,3 +159,19 @@ def test_gram_long_k(tc):
     # K = 2048: the TMA tile drains its TMEM accumulator into float32 registers every 256 k,
     # which keeps the error inside the float32 bound (a single TMEM accumulation does not)
     test_gram(tc, 2048)
+
+
+def test_bounded_wait_times_out_cleanly():
+    # Failure detection without a GPU fault: a short bounded wait on an mbarrier that nothing
+    # completes runs out in every CTA; each one reports INFO_DEVICE_TIMEOUT, frees its tensor
+    # memory and returns.  The context stays usable: tensor-core work runs right after it
+    # (2 x 148 CTAs so that every SM's TMEM is taken and freed at least once).
+    from qrb200 import _lib
+    h = kit()
+    h.qrbt_timeout_probe.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_void_p]
+    blocks = 296
+    info = torch.zeros(blocks, dtype=torch.int32, device="cuda")
+    assert h.qrbt_timeout_probe(info.data_ptr(), blocks, 4096, stream()) == 0
+    torch.cuda.synchronize()
+    assert bool((info == _lib.INFO_DEVICE_TIMEOUT).all())
+    test_gram(2, 256)

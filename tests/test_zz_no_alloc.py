@@ -75,3 +75,44 @@ def test_noalloc_bf16_and_limit():
     rc = _lib.lib().qrb200_geqrf_batched_noalloc(1, 1, 1, 1, 1, 2048, _lib.QRB200_F32, None)
     assert rc == _lib.QRB200_ERR_SCRATCH_LIMIT
     assert "scratch" in _lib.status_string(rc)
+
+
+def test_noalloc_largest_order_runs():
+    # n = 1826 is the largest order whose working set fits the array with the default block
+    # options (1827 is rejected, see tests/test_abi.py); one such matrix factors and passes
+    from qrb200 import _lib
+    n = _lib.NOALLOC_MAX_N_DEFAULT
+    g = torch.Generator(device="cuda").manual_seed(3)
+    A = torch.randn(1, n, n, device="cuda", generator=g)
+    H, tau, info = _noalloc(A)
+    torch.cuda.synchronize()
+    assert int(info.sum()) == 0
+    _, _, _, _, passed = checker.check(A, H, tau)
+    assert bool(passed.all())
+
+
+def test_noalloc_allocates_nothing():
+    # after a warm-up call (which may load kernel modules), a call changes neither the
+    # device's free memory nor torch's allocator statistics
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn(24, 256, 256, device="cuda", generator=g)
+    out = _noalloc(A)
+    torch.cuda.synchronize()
+    del out
+    from qrb200 import _lib
+    n, batch = 256, 24
+    H = torch.empty_like(A)
+    tau = torch.empty(batch, n, device="cuda")
+    info = torch.empty(batch, dtype=torch.int32, device="cuda")
+    free1, _ = torch.cuda.mem_get_info()
+    st1 = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
+    rc = _lib.lib().qrb200_geqrf_batched_noalloc(
+        A.data_ptr(), H.data_ptr(), tau.data_ptr(), info.data_ptr(), batch, n, _lib.QRB200_F32,
+        torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert rc == _lib.QRB200_OK
+    free2, _ = torch.cuda.mem_get_info()
+    st2 = torch.cuda.memory_stats().get("allocation.all.allocated", 0)
+    assert free2 == free1, (free1, free2)
+    assert st2 == st1
+    assert int(info.sum()) == 0
