@@ -6,12 +6,22 @@ float32 matrices (256 each of dense / ill-conditioned / rank-deficient / row-sca
 near-rank-deficient / upper-triangular; seeded synthetic data, seed 3 + rank).  Inputs are
 1.5 GiB per step, larger than the 126 MB L2, so no flush is needed between steps.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qrb200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl qrb200|reference] [--quick]
 
 N > 1 is launched by torchrun (one rank per GPU, NCCL); every rank factors its own 1536
 matrices (weak scaling, no collective on the data path) and the time is the max over ranks.
-``--impl reference`` times the reference algorithm's CPU restatement (oracle port) on the
-host cores, rank 0 only.
+Every output of the timed steps is gated afterwards in float64 on the device.
+
+Besides the headline the line carries the other BASELINE.json configurations, each measured
+on the device: ``c2`` (small n, leading dims (128, 128, n, n)), ``c4`` (64 matrices of
+2048 x 2048, sigma down to 1e-12) and ``c5`` (the fixed global batch of 65536 bf16
+256 x 256 matrices sharded over the ranks, factorization and NCCL all-gather timed apart),
+the host-link roof of the end-to-end path, the reference's own ``custom_kernel`` and
+``torch.geqrf`` on the host cores and on the GPU (context), and the roofline.
+
+``--impl reference`` times the reference's own ``custom_kernel`` (pure PyTorch, installed
+unmodified under baseline/_ref) on the host cores of this node, rank 0 only; without that
+install it falls back to the numpy restatement under oracle/ (kind "port").
 """
 from __future__ import annotations
 
@@ -30,11 +40,16 @@ for _p in (REPO, REPO / "qr-contest_b200"):
     if str(_p) not in sys.path:
         sys.path.insert(0, str(_p))
 
-import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "batched fp32 QR matrices/s at n=512 (heterogeneous 6-class batch)"
 UNIT = "matrices/s"
+REF_DIR = REPO / "baseline" / "_ref"
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of every kernel of one library
+# call, per matrix, from an ncu capture of the n = 512 heterogeneous configuration at 256
+# matrices (profiles/dram_traffic_all_kernels_n512_b256.md); None until captured
+TRAFFIC_PER_MATRIX = {}
 
 
 def parse():
@@ -48,6 +63,8 @@ def parse():
     p.add_argument("--cpu-sample", type=int, default=16, help="matrices per class (CPU leg)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--quick", action="store_true",
+                   help="headline only: no extra configurations, GPU context or gates")
     p.add_argument("--profile-run", action="store_true",
                    help="one warm-up call and one measured call of the library, nothing else "
                         "(the command the ncu summaries under profiles/ are taken on)")
@@ -97,51 +114,6 @@ def family_flops(n: int) -> dict:
     f["q_apply"] = 2.0 * n ** 3         # two passes of X R^{-1} (R^{-1} upper triangular)
     f["closure"] = 1.0 * n ** 3         # upper triangle of Q^T A
     return f
-
-
-def family_bytes(n: int) -> dict:
-    """Algorithmic HBM bytes of each family per matrix (float32 working set)."""
-    nb = nb_for(n)
-    b = {k: 0.0 for k in family_flops(n)}
-    for k0 in range(0, n, nb):
-        w = min(nb, n - k0)
-        m = n - k0
-        t = n - k0 - w
-        k1 = k0 + w
-        b["lu_panel"] += 4.0 * (m * w + n * w + t * w)
-        b["chart_panel"] += 4.0 * (m * w + m * w + t * w)
-        b["chol_panel"] += 2 * 4.0 * (m * w + m * w)
-        b["lu_trail"] += 4.0 * (2 * t * t + t * w + w * t)
-        b["chart_trail"] += 4.0 * (2 * t * t + t * w + w * t)
-        b["chol_trail"] += 2 * 4.0 * (t * t + 2 * t * w + 2 * t * k1)  # G lower half, L_G^-1
-    # two-level Cholesky and chart eliminations (the library's default block of 128 columns
-    # when 32-wide panels are used and n > 128): C moves once per panel only inside the block
-    # strips, and once per block for the rest
-    blk = 128
-    if nb == 32 and n > blk and n % 4 == 0:
-        chol = chart = 8.0 * n * n  # chart: the frame copied into the working buffer once
-        for kb in range(0, n, blk):
-            ke = min(n, kb + blk)
-            for k0 in range(kb, ke, nb):
-                w = min(nb, n - k0)
-                k1 = k0 + w
-                c = ke - k1
-                # Cholesky: block columns of every row below (lower part), L_G^-1 rows in block
-                chol += 8.0 * ((n - k1) * c - c * (c - 1) / 2) + 4.0 * ((n - k1) * w + w * c)
-                chol += 4.0 * ((ke - k1) * k0 + (ke - k0) * k1 + (ke - k0) * w + w * k1)
-                # chart: block columns of every row below, block rows right of the block
-                chart += 8.0 * ((n - k1) * c + c * (n - ke)) + 4.0 * ((n - k1) * w + w * (n - k1))
-            t2, K = n - ke, ke - kb
-            if t2 > 0:
-                chol += 8.0 * t2 * (t2 + 1) / 2 + 4.0 * 2 * K * t2           # trailing triangle
-                chol += 4.0 * (t2 * kb + t2 * ke + t2 * K + K * ke)          # L_G^-1 rows below
-                chart += 8.0 * t2 * t2 + 4.0 * 2 * K * t2
-        b["chol_trail"] = 2 * chol
-        b["chart_trail"] = chart
-    b["gram"] = 2 * 4.0 * (n * n + n * n / 2)
-    b["q_apply"] = 4.0 * (2 * n * n + n * n / 2) + 4.0 * (3 * n * n + n * n / 2)
-    b["closure"] = 4.0 * (2 * n * n + n * n / 2)
-    return b
 
 
 # ----------------------------------------------------------------------------------------
@@ -209,14 +181,17 @@ def dist_setup():
     return world, rank, local
 
 
-def cpu_port_rate(A_cpu: torch.Tensor, threads: int):
-    """Time the numpy oracle (the reference algorithm restated) on host cores."""
-    from oracle import qr_oracle
-    torch.set_num_threads(threads)
-    A = A_cpu.numpy()
-    t0 = time.perf_counter()
-    qr_oracle.custom_kernel_np(A)
-    return A.shape[0] / (time.perf_counter() - t0)
+
+def load_reference():
+    """The reference's own module (reflection_no_reflectors, pure PyTorch) from its unmodified
+    install under baseline/_ref, or None when it is not installed."""
+    if not (REF_DIR / "reflection_no_reflectors.py").exists():
+        return None
+    sys.dont_write_bytecode = True
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    import reflection_no_reflectors as ref
+    return ref
 
 
 def cpu_sample(n: int, per_class: int, seed: int = 3):
@@ -224,6 +199,25 @@ def cpu_sample(n: int, per_class: int, seed: int = 3):
     g = G._gen(seed, "cpu")
     parts = [G.make_class(c, per_class, n, g, "cpu").float() for c in G.CLASSES]
     return torch.cat(parts)
+
+
+def cpu_rate(fn, A, reps: int = 1):
+    """matrices/s of ``fn(A)`` on the host (one untimed call first)."""
+    fn(A)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        fn(A)
+    return reps * A.shape[0] / (time.perf_counter() - t0)
+
+
+def cpu_name() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
 def config(args, world):
@@ -234,22 +228,63 @@ def config(args, world):
             "l2": "inputs larger than L2 (1.5 GiB per step), no flush"}
 
 
+def dev_time(fn, dev, reps: int, warm: int = 1, world: int = 1):
+    """Mean device milliseconds of ``fn()`` over ``reps`` calls (CUDA events on the current
+    stream, barrier + synchronize on both sides, max over ranks)."""
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    st = torch.cuda.current_stream(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        fn()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    ms = e0.elapsed_time(e1) / reps
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
 # ----------------------------------------------------------------------------------------
 def run_reference(args):
+    """The reference arm: the reference's own custom_kernel on the host cores (rank 0)."""
     world, rank, _ = dist_setup()
     if rank != 0:
         return
-    cores = os.cpu_count() or 1
+    # torch's default thread count is every core of the host; calling torch.set_num_threads
+    # (even with the same value) makes MKL's batched LU under torch.linalg.lu fail here
+    cores = torch.get_num_threads()
     per = 2
     A = cpu_sample(args.n, per, seed=3)
-    from oracle import qr_oracle
-    torch.set_num_threads(cores)
+    ref = load_reference()
+    if ref is not None:
+        kind = "reference"
+
+        def fn(X):
+            return ref.custom_kernel(X.clone())
+        what = ("the reference's own reflection_no_reflectors.custom_kernel (unmodified, "
+                "baseline/_ref) on torch CPU")
+    else:
+        from oracle import qr_oracle
+        kind = "port"
+
+        def fn(X):
+            return qr_oracle.custom_kernel_np(X.numpy())
+        what = "the numpy restatement of reflection_no_reflectors.custom_kernel (oracle/)"
     for _ in range(args.warmup):
-        qr_oracle.custom_kernel_np(A.numpy())
+        fn(A)
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        qr_oracle.custom_kernel_np(A.numpy())
+        fn(A)
         times.append(time.perf_counter() - t0)
     rate = A.shape[0] * len(times) / sum(times)
     line = {"metric": METRIC, "value": rate, "unit": UNIT, "impl": "reference",
@@ -257,18 +292,249 @@ def run_reference(args):
             "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config(args, world),
-            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
+            "cpu_baseline": {"value": rate, "unit": UNIT, "cores": cores, "kind": kind,
+                             "cpu": cpu_name(),
+                             "scope": "the host CPU of this node, run once (rank 0 only "
+                                      "under torchrun; the other ranks do no work)",
                              "sample": f"{A.shape[0]} matrices per step ({per} per class, "
-                                       f"n={args.n}, seed 3) through the numpy restatement "
-                                       "of reflection_no_reflectors.custom_kernel"},
+                                       f"n={args.n}, seed 3) through {what}"},
             "e2e": {"value": rate, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------------------
+def roofline(value_per_gpu: float, n: int, fams: dict, B: int) -> dict:
+    """Roofline of the headline: the whole call's 7 n^3 flops per matrix against the 3xTF32
+    tensor roof (n = 512 runs at ~447 flop per algorithmic byte, far above the ridge), with
+    every kernel family's own algorithmic flops against the same roof beside it."""
+    hbm, bf16, src = measured_peaks()
+    sus = None
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        sus = json.loads(p.read_text()).get("bf16_tflops_sustained")
+    tc_peak = bf16 / 2 / 3  # TF32 runs at half the bf16 rate; 3 products per float32 product
+    achieved = value_per_gpu * algo_flops(n) / 1e12
+    roof = {"bound": "tensor", "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s",
+            "frac": achieved / tc_peak,
+            "kernel": "whole qrb200_geqrf_batched call (all kernel families, 7 n^3 per matrix)",
+            "peak_source": (f"{src} MEASURED_PEAKS.json bf16 {bf16} TF/s (burst) / 2 (TF32) "
+                            "/ 3 (3xTF32 products)")}
+    if sus:
+        roof["frac_of_sustained"] = achieved / (float(sus) / 6)
+    alg_bytes = algo_bytes(n) * B
+    tpm = TRAFFIC_PER_MATRIX.get(n)
+    roof["algorithmic_bytes_per_step"] = alg_bytes
+    roof["traffic"] = tpm * B if tpm else None
+    if tpm:
+        roof["traffic_unit"] = ("DRAM bytes per step: ncu dram__bytes_read.sum + "
+                                "dram__bytes_write.sum over every kernel of a 256-matrix call, "
+                                "scaled to the batch")
+        roof["waste"] = tpm / algo_bytes(n)
+    roof["hbm_frac_of_algorithmic_bytes"] = value_per_gpu * algo_bytes(n) / 1e9 / hbm
+    ff = family_flops(n)
+    total = sum(fams.values()) or 1.0
+    per = {}
+    for k, ms in fams.items():
+        if ms <= 0:
+            continue
+        tf = ff.get(k, 0.0) * B / (ms / 1000.0) / 1e12
+        per[k] = {"ms": round(ms, 4), "share": round(ms / total, 4),
+                  "tflops": round(tf, 3), "frac": round(tf / tc_peak, 4)}
+    roof["families"] = per
+    dom = max(per, key=lambda k: per[k]["ms"]) if per else None
+    roof["dominant_family"] = dict(per[dom], name=dom) if dom else None
+    return roof
+
+
+def measure_host_link(Ah, out, dev, world):
+    """Copy-engine roof of the end-to-end path: the step's upload and download bytes copied
+    between the same pinned host buffers and the device, alone and both directions at once,
+    on every rank at the same time (max over ranks)."""
+    import torch.distributed as dist
+    dA = torch.empty(Ah.shape, dtype=Ah.dtype, device=dev)
+    dO = [torch.empty(t.shape, dtype=t.dtype, device=dev) for t in out]
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def timed(up: bool, down: bool):
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        if up:
+            with torch.cuda.stream(s1):
+                dA.copy_(Ah, non_blocking=True)
+        if down:
+            with torch.cuda.stream(s2):
+                for h, d in zip(out, dO):
+                    h.copy_(d, non_blocking=True)
+        torch.cuda.synchronize(dev)
+        ms = (time.perf_counter() - t0) * 1e3
+        if world > 1:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    timed(True, True)
+    up, down, both = timed(True, False), timed(False, True), timed(True, True)
+    ub = Ah.numel() * Ah.element_size()
+    db = sum(t.numel() * t.element_size() for t in out)
+    del dA, dO
+    return {"h2d_gbs_per_rank": ub / up / 1e6, "d2h_gbs_per_rank": db / down / 1e6,
+            "both_directions_ms": both, "ranks_copying_at_once": world,
+            "matrices_per_s_bound": world * Ah.shape[0] / (both / 1e3),
+            "method": "host wall clock around cudaMemcpyAsync between the pinned step buffers "
+                      "and device memory, after a barrier, max over ranks"}
+
+
+def measure_c2(dev):
+    """(128, 128, n, n) float32 iid N(0,1), n = 32 (seed 1) and 128 (seed 2)."""
+    import qrb200
+    from qrb200 import checker
+    from qrb200 import generators as G
+    hbm, bf16, _ = measured_peaks()
+    res = {}
+    for n, seed in ((32, 1), (128, 2)):
+        A = G.gaussian((128, 128, n, n), seed=seed, device=dev)
+        ws = torch.empty(qrb200.api.workspace_bytes(A.numel() // (n * n), n), dtype=torch.uint8,
+                         device=dev)
+        out = {}
+
+        def step():
+            out["r"] = qrb200.geqrf(A, workspace=ws)
+        ms = dev_time(step, dev, reps=5, warm=3)
+        H, tau, info = out["r"]
+        b = A.numel() // (n * n)
+        rate = b / (ms / 1e3)
+        gbs = rate * algo_bytes(n) / 1e9
+        tf = rate * algo_flops(n) / 1e12
+        gates = checker.summary(A.reshape(-1, n, n)[:512], H.reshape(-1, n, n)[:512],
+                                tau.reshape(-1, n)[:512])
+        res[f"n{n}"] = {"shape": [128, 128, n, n], "matrices_per_s": rate, "ms": ms,
+                        "hbm_gbs_algorithmic": gbs, "hbm_frac": gbs / hbm,
+                        "tflops_7n3": tf, "tensor_frac": tf / (bf16 / 6),
+                        "info_nonzero": int((info != 0).sum()), "gates_first_512": gates}
+        del A, ws, H, tau, info, out
+    return res
+
+
+def measure_c4(dev):
+    """64 matrices of 2048 x 2048, U diag(sigma) V^T, sigma to 1e-12."""
+    import qrb200
+    from qrb200 import checker
+    from qrb200 import generators as G
+    _, bf16, _ = measured_peaks()
+    n, b = 2048, 64
+    A = G.large_illcond(b, n, seed=4, device=dev)
+    ws = torch.empty(qrb200.api.workspace_bytes(b, n), dtype=torch.uint8, device=dev)
+    out = {}
+
+    def step():
+        out["r"] = qrb200.geqrf(A, workspace=ws)
+    ms = dev_time(step, dev, reps=2, warm=1)
+    H, tau, info = out["r"]
+    rate = b / (ms / 1e3)
+    tf = rate * algo_flops(n) / 1e12
+    gates = checker.summary(A[:4], H[:4], tau[:4], chunk=2)
+    r = {"matrices": b, "n": n, "ms": ms, "matrices_per_s": rate, "tflops_7n3": tf,
+         "tensor_frac": tf / (bf16 / 6), "info_nonzero": int((info != 0).sum()),
+         "gates_first_4": gates}
+    del A, ws, H, tau, info, out
+    return r
+
+
+def measure_c5(dev, rank, world):
+    """a fixed global batch of 65536 bf16 256 x 256 matrices (six classes,
+    round robin, rank parameter 128), sharded contiguously over the ranks; factors computed in
+    float32 and returned in bf16; then H and tau all-gathered over NCCL (timed apart)."""
+    import qrb200
+    from qrb200 import checker
+    from qrb200 import generators as G
+    _, bf16, _ = measured_peaks()
+    n, gb = 256, 65536
+    A, lo = G.sweep_shard(gb, n, rank, world, seed=5, device=dev, dtype=torch.bfloat16)
+    b = A.shape[0]
+    ws = torch.empty(qrb200.api.workspace_bytes(b, n), dtype=torch.uint8, device=dev)
+    out = {}
+
+    def step():
+        out["r"] = qrb200.geqrf(A, workspace=ws)
+    ms = dev_time(step, dev, reps=2, warm=1, world=world)
+    H, tau, info = out["r"]
+    del ws
+    bad = int((info != 0).sum())
+    # float32 factors of a sample of this shard's (bf16) inputs, gated in float64
+    As = A[:96].float()
+    Hs, ts, _ = qrb200.geqrf(As)
+    gates = checker.summary(As, Hs, ts)
+    r = {"global_batch": gb, "n": n, "dtype": "bf16 in/out, float32 compute",
+         "per_rank": b, "factor_ms_max_over_ranks": ms,
+         "matrices_per_s": gb / (ms / 1e3), "tflops_7n3": gb / (ms / 1e3) * algo_flops(n) / 1e12,
+         "tensor_frac_per_gpu": gb / world / (ms / 1e3) * algo_flops(n) / 1e12 / (bf16 / 6),
+         "info_nonzero_rank0": bad, "gates_rank0_sample96_fp32": gates,
+         "scaling": "strong (fixed global batch)"}
+    if world > 1:
+        import torch.distributed as dist
+        Hall = torch.empty(gb, n, n, dtype=H.dtype, device=dev)
+        tall = torch.empty(gb, n, dtype=tau.dtype, device=dev)
+
+        def gather():
+            dist.all_gather_into_tensor(Hall, H)
+            dist.all_gather_into_tensor(tall, tau)
+        gms = dev_time(gather, dev, reps=2, warm=1, world=world)
+        moved = (world - 1) * b * (n * n + n) * 2
+        r.update({"allgather_ms_max_over_ranks": gms,
+                  "allgather_bytes_received_per_rank": moved,
+                  "allgather_gbs_per_rank": moved / (gms / 1e3) / 1e9,
+                  "limiter": "all-gather" if gms > ms else "factorization"})
+        del Hall, tall
+    else:
+        r["allgather_ms_max_over_ranks"] = None
+    del A, H, tau, info, out, As, Hs, ts
+    return r
+
+
+def gpu_context(A, dev):
+    """Context (not a baseline arm): the reference's own custom_kernel and torch.geqrf run on
+    this B200 on the first 256 matrices of the headline batch."""
+    res = {}
+    S = A[:256].contiguous()
+    ref = load_reference()
+    if ref is not None:
+        ms = dev_time(lambda: ref.custom_kernel(S), dev, reps=1, warm=1)
+        res["reference_custom_kernel_gpu"] = {"matrices_per_s": S.shape[0] / (ms / 1e3),
+                                              "ms": ms, "matrices": S.shape[0]}
+    ms = dev_time(lambda: torch.geqrf(S), dev, reps=1, warm=1)
+    res["torch_geqrf_gpu"] = {"matrices_per_s": S.shape[0] / (ms / 1e3), "ms": ms,
+                              "matrices": S.shape[0]}
+    return res
+
+
+def cpu_context(n: int, per_class: int):
+    """The reference's own custom_kernel (cpu_baseline) and torch.geqrf on the host cores."""
+    cores = torch.get_num_threads()  # the default: every core (see run_reference)
+    As = cpu_sample(n, per_class, seed=3)
+    sample = f"{As.shape[0]} matrices ({per_class} per class, n={n}, seed 3)"
+    ref = load_reference()
+    if ref is not None:
+        rate = cpu_rate(lambda X: ref.custom_kernel(X.clone()), As)
+        base = {"value": rate, "unit": UNIT, "cores": cores, "kind": "reference",
+                "cpu": cpu_name(),
+                "sample": sample + " through the reference's own "
+                          "reflection_no_reflectors.custom_kernel (unmodified, baseline/_ref)"}
+    else:
+        from oracle import qr_oracle
+        rate = cpu_rate(lambda X: qr_oracle.custom_kernel_np(X.numpy()), As)
+        base = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port", "cpu": cpu_name(),
+                "sample": sample + " through the numpy restatement of the reference pipeline"}
+    geq = cpu_rate(lambda X: torch.geqrf(X), As, reps=2)
+    return base, {"value": geq, "unit": UNIT, "cores": cores, "sample": sample}
+
+
 def run_qrb(args):
     import qrb200
-    from qrb200 import _lib, api
+    from qrb200 import _lib, checker
     from qrb200 import generators as G
 
     world, rank, local = dist_setup()
@@ -280,7 +546,7 @@ def run_qrb(args):
     torch.cuda.set_device(dev)
     n, B = args.n, args.batch
     A = G.heterogeneous(B, n, seed=3 + rank, device=dev)
-    ws = torch.empty(api.workspace_bytes(B, n), dtype=torch.uint8, device=dev)
+    ws = torch.empty(qrb200.api.workspace_bytes(B, n), dtype=torch.uint8, device=dev)
     torch.cuda.synchronize(dev)
 
     def barrier():
@@ -327,7 +593,17 @@ def run_qrb(args):
         ms = float(t.item())
     value = world * B * args.steps / (ms / 1000.0)
 
-    # ---- roofline: per-family device time with CUDA events on the launch stream ----
+    # ---- every output of the last timed step, gated in float64 on the device ----
+    gates = None
+    if not args.quick:
+        gates = checker.summary(A, H, tau)
+        gates["info_nonzero"] = int((info != 0).sum())
+        gates["what"] = ("all matrices of the last timed step on this rank: fp64 "
+                         "householder_product, ||R - Q^T A||_1/||A||_1 / (20 n eps32), "
+                         "||Q^T Q - I||_1 / (100 n eps32), tau in [1, 2] +- 1e-6")
+    del H, tau, info
+
+    # ---- per-family device time with CUDA events on the launch stream ----
     fams = {}
     reps = 2
     for _ in range(reps):
@@ -340,35 +616,8 @@ def run_qrb(args):
         assert rc == 0, rc
         for k, v in f.items():
             fams[k] = fams.get(k, 0.0) + v / reps
-    dom = max(fams, key=fams.get)
-    hbm, bf16, src = measured_peaks()
-    ff = family_flops(n)[dom] * B
-    fb = family_bytes(n)[dom] * B
-    t_dom = fams[dom] / 1000.0
-    tc_peak = bf16 / 2 / 3  # 3xTF32 roof: TF32 rate is half the bf16 rate, three products
-    t_tc, t_hbm = ff / (tc_peak * 1e12), fb / (hbm * 1e9)
-    if t_tc >= t_hbm:
-        roof = {"bound": "tensor", "achieved": ff / t_dom / 1e12, "peak": tc_peak,
-                "unit": "TFLOP/s"}
-    else:
-        roof = {"bound": "hbm", "achieved": fb / t_dom / 1e9, "peak": hbm, "unit": "GB/s"}
-    roof["frac"] = roof["achieved"] / roof["peak"]
-    # DRAM bytes per matrix of the chol_trail kernels from an ncu capture of the same
-    # configuration at 256 matrices (dram__bytes_read.sum + dram__bytes_write.sum summed over
-    # the family's launches), scaled to the batch; writes that were still in L2 when each
-    # profiled launch ended are not in it
-    traffic_per_matrix = {("chol_trail", 512): 9.54e6}.get((dom, n))
-    roof["traffic"] = traffic_per_matrix * B if traffic_per_matrix else None
-    if traffic_per_matrix:
-        roof["traffic_unit"] = "bytes per step (ncu, 256-matrix capture scaled to the batch)"
-    roof["kernel"] = dom
-    roof["peak_source"] = (f"{src} MEASURED_PEAKS.json: bf16 {bf16} TF/s / 2 (TF32) / 3 "
-                           f"(3xTF32), HBM {hbm} GB/s")
-    roof["family_ms_per_step"] = {k: round(v, 4) for k, v in fams.items()}
-    roof["family_share"] = {k: round(v / sum(fams.values()), 4) for k, v in fams.items()}
-    whole_tflops = value / world * algo_flops(n) / 1e12
-    roof["pipeline_tflops_7n3"] = whole_tflops
-    roof["pipeline_frac_of_3xtf32_roof"] = whole_tflops / tc_peak
+    del Hh, th, inf
+    roof = roofline(value / world, n, fams, B)
 
     # ---- e2e through the public API with pinned host buffers ----
     e2e = None
@@ -406,15 +655,29 @@ def run_qrb(args):
                "path": "pinned host A -> qrb200.api.geqrf_host (C ABI "
                        "qrb200_geqrf_batched_host: sub-batches over 3 streams, copies overlapped "
                        "with kernels) -> pinned host H/tau/info"}
+        if not args.quick:
+            link = measure_host_link(Ah, out, dev, world)
+            link["e2e_frac_of_link_bound"] = e2e["value"] / link["matrices_per_s_bound"]
+            e2e["host_link"] = link
+        del Ah, out
+
+    extra = {}
+    if not args.quick:
+        del ws
+        torch.cuda.empty_cache()
+        extra["c5"] = measure_c5(dev, rank, world)
+        torch.cuda.empty_cache()
+        if world == 1:
+            extra["c2"] = measure_c2(dev)
+            torch.cuda.empty_cache()
+            extra["c4"] = measure_c4(dev)
+            torch.cuda.empty_cache()
+            extra["gpu_context"] = gpu_context(A, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cores = os.cpu_count() or 1
-        As = cpu_sample(n, args.cpu_sample, seed=3)
-        rate = cpu_port_rate(As, cores)
-        cpu = {"value": rate, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{As.shape[0]} matrices ({args.cpu_sample} per class, n={n}, "
-                         "seed 3) through the numpy restatement of the reference pipeline"}
+        cpu, geq = cpu_context(n, args.cpu_sample)
+        extra["geqrf_cpu"] = geq
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -422,9 +685,10 @@ def run_qrb(args):
                 "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic",
                 "config": config(args, world), "roofline": roof, "cpu_baseline": cpu,
-                "e2e": e2e, "gpu_launches": launches, "clocks": clk,
+                "e2e": e2e, "gpu_launches": launches, "clocks": clk, "gates": gates,
                 "gflops_4n3_per_s": value * 4 * n ** 3 / 3 / 1e9,
                 "device": torch.cuda.get_device_name(dev)}
+        line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -101,3 +101,37 @@ def large_illcond(b: int, n: int, seed: int = 4, device="cpu", dtype=torch.float
         j = min(b, i + chunk)
         out[i:j] = make_class("illcond", j - i, n, g, device, sigma_min_exp=-12.0).to(dtype)
     return out
+
+
+C5_BLOCK = 1024  # matrices per independently seeded block of the C5 sweep
+
+
+def sweep_shard(global_batch: int, n: int, rank: int, world: int, seed: int = 5,
+                device="cpu", dtype=torch.bfloat16, block: int = C5_BLOCK):
+    """This rank's slice of the 8-GPU sweep batch (the six classes regenerated at order n,
+    rank parameter n // 2, class = global index mod 6), generated on ``device``.
+
+    Rank g owns the contiguous global slice ``[g * ceil(b / G), ...)``.  The global batch is
+    cut into blocks of ``block`` matrices, block j seeded with ``seed + j * block`` (the
+    seed plus the block's global offset), so every rank builds only its own slice and the
+    global batch is the same for every world size.  Returns ``(shard, first_global_index)``.
+    """
+    per = -(-global_batch // world)
+    lo = min(global_batch, rank * per)
+    hi = min(global_batch, lo + per)
+    out = torch.empty(hi - lo, n, n, dtype=dtype, device=device)
+    j0 = lo // block
+    for j in range(j0, -(-hi // block)):
+        b0, b1 = j * block, min(global_batch, (j + 1) * block)
+        s0, s1 = max(b0, lo), min(b1, hi)
+        if s0 >= s1:
+            continue
+        g = _gen(seed + b0, device)
+        blk = torch.empty(b1 - b0, n, n, dtype=dtype, device=device)
+        for c in range(6):
+            # global index i has class i mod 6: inside the block that is offset (c - b0) mod 6
+            idx = torch.arange((c - b0) % 6, b1 - b0, 6, device=device)
+            if idx.numel():
+                blk[idx] = make_class(CLASSES[c], idx.numel(), n, g, device).to(dtype)
+        out[s0 - lo:s1 - lo] = blk[s0 - b0:s1 - b0]
+    return out, lo

@@ -14,16 +14,33 @@ TIGHT = ("dense_", "smoke_", "small_", "lead_", "n1", "n2", "identity", "neg_ide
 LOOSE = ("illcond_",)
 
 
+def loose_tol(n: int) -> float:
+    """|tau - tau_ref| bound for the ill-conditioned class (cond(A) = 1e6): the frame's
+    trailing columns are only determined to about cond(A) * eps32 ~ 0.1, and at n = 512 the
+    oracle and the reference differ by up to 0.022 in tau."""
+    return 2e-2 if n <= 64 else 5e-2
+
+
 def names():
     return sorted(p.stem for p in HERE.glob("*.npz"))
 
 
+# the 8-GPU sweep fixture: bf16 inputs of the six classes in round-robin order (class =
+# index mod 6); only dense (0) and upper-triangular (5) are determined elementwise
+C5_TIGHT = (0, 5)
+
+
 def load(name):
     z = np.load(HERE / f"{name}.npz")
-    return {"A": z["A"], "H": z["H"], "tau": z["tau"], "dtype": str(z["dtype"])}
+    d = {"A": z["A"], "H": z["H"], "tau": z["tau"], "dtype": str(z["dtype"])}
+    if "H32" in z.files:  # the reference's float32 factors of the same (bf16) inputs
+        d["H32"], d["tau32"] = z["H32"], z["tau32"]
+    return d
 
 
 def kind(name):
+    if name.startswith("c5_"):
+        return "c5"
     if name.startswith("bf16"):
         return "bf16"
     if any(name.startswith(t) for t in TIGHT):

@@ -19,6 +19,23 @@ def test_oracle_matches_reference(name):
     fx = F.load(name)
     A = fx["A"]
     kind = F.kind(name)
+    if kind == "c5":
+        # bf16 inputs of all six classes: the oracle's float32 factors pass the gates, match
+        # the reference's float32 factors where they are determined (dense, upper-triangular)
+        # and, rounded to bf16, its bf16 outputs there
+        At = torch.from_numpy(A)
+        H, tau = O.custom_kernel_np(A)
+        f, o, ftol, otol, passed = checker.check(At, torch.from_numpy(H), torch.from_numpy(tau))
+        assert bool(passed.all()), (f / ftol, o / otol)
+        _, _, _, _, ref_pass = checker.check(At, torch.from_numpy(fx["H32"]),
+                                             torch.from_numpy(fx["tau32"]))
+        assert bool(ref_pass.all())
+        for i in F.C5_TIGHT:
+            np.testing.assert_allclose(H[i], fx["H32"][i], rtol=1e-4, atol=1e-4)
+            np.testing.assert_allclose(tau[i], fx["tau32"][i], rtol=0, atol=1e-4)
+            Hb = torch.from_numpy(H[i]).to(torch.bfloat16).float().numpy()
+            np.testing.assert_allclose(Hb, fx["H"][i], rtol=2 ** -7, atol=1e-3)
+        return
     if kind == "bf16":
         H, tau = O.custom_kernel(torch.from_numpy(A).to(torch.bfloat16))
         H, tau = H.float().numpy(), tau.float().numpy()
@@ -37,7 +54,7 @@ def test_oracle_matches_reference(name):
         np.testing.assert_allclose(H, fx["H"], rtol=1e-4, atol=1e-4)
         np.testing.assert_allclose(tau, fx["tau"], rtol=0, atol=1e-4)
     elif kind == "loose":
-        np.testing.assert_allclose(tau, fx["tau"], rtol=0, atol=2e-2)
+        np.testing.assert_allclose(tau, fx["tau"], rtol=0, atol=F.loose_tol(A.shape[-1]))
 
 
 def test_lu_pivots_match_torch():
