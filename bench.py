@@ -415,6 +415,27 @@ def measure_c2(dev):
                         "hbm_gbs_algorithmic": gbs, "hbm_frac": gbs / hbm,
                         "tflops_7n3": tf, "tensor_frac": tf / (bf16 / 6),
                         "info_nonzero": int((info != 0).sum()), "gates_first_512": gates}
+        # the other side of the fused / staged crossover on the same batch (evidence for it)
+        from qrb200 import _lib
+        small = 64
+        _lib.set_small_n(0 if n <= small else 128)
+        try:
+            ws2 = torch.empty(qrb200.api.workspace_bytes(b, n), dtype=torch.uint8, device=dev)
+            ms2 = dev_time(lambda: qrb200.geqrf(A, workspace=ws2), dev, reps=3, warm=1)
+        finally:
+            _lib.set_small_n(small)
+        res[f"n{n}"]["other_path"] = {"path": "staged kernels" if n <= small else
+                                      "fused one-CTA-per-matrix kernel",
+                                      "ms": ms2, "matrices_per_s": b / (ms2 / 1e3)}
+        res[f"n{n}"]["path"] = "fused one-CTA-per-matrix kernel" if n <= small else "staged kernels"
+        Hh = torch.empty_like(A)
+        th = torch.empty(b, n, device=dev)
+        inf = torch.zeros(b, dtype=torch.int32, device=dev)
+        rc, f = _lib.geqrf_batched_timed(A.data_ptr(), Hh.data_ptr(), th.data_ptr(),
+                                         inf.data_ptr(), b, n, _lib.QRB200_F32, ws.data_ptr(),
+                                         ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+        res[f"n{n}"]["family_ms"] = {k: round(v, 4) for k, v in f.items() if v > 0}
+        del ws2, Hh, th, inf
         del A, ws, H, tau, info, out
     return res
 

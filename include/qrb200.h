@@ -70,6 +70,18 @@ int qrb200_geqrf_batched(const void* A, void* H, void* tau, int32_t* info, int64
                          int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
                          void* stream);
 
+/* qrb200_geqrf_batched plus the explicit orthogonal factor
+ *   Q     [batch][n][n]  output, element type `dtype`: Q = householder_product(H, tau)
+ * Replaces the consumer-side reconstruction torch.linalg.householder_product(H, tau) (LAPACK
+ * orgqr, the use the reference documents in README.md:125-127): the chart factors
+ * I - Q_frame S = Y (T Y^T) (reflection_no_reflectors.py:86-176), so the product of the
+ * reflectors is the frame (:81) with column k scaled by the sign s_k, and it is written
+ * straight from the frame the pipeline already holds (n^2 work instead of O(n^3)).
+ * Same workspace, status codes and info bits as qrb200_geqrf_batched; Q may not be NULL. */
+int qrb200_geqrf_batched_q(const void* A, void* H, void* tau, void* Q, int32_t* info,
+                           int64_t batch, int32_t n, int32_t dtype, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Same computation as qrb200_geqrf_batched, with every kernel launch bracketed by CUDA
  * events on `stream`; blocks until the stream is idle and writes the summed device time
  * (milliseconds) of each kernel family into family_ms[0 .. qrb200_num_families()-1].

@@ -452,21 +452,50 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
 
 template <typename T>
 static void launch_small(const T* A, T* H, T* tau, int* info, int64_t cb, int n, cudaStream_t st,
-                         Prof* prof) {
+                         Prof* prof, T* Q) {
   QRB_LAUNCH(prof, F_SMALL,
              if (n <= 32) small_qr_kernel<32, 128, T>
-                 <<<(unsigned)cb, 128, small_smem_bytes<32, 128>(), st>>>(A, H, tau, info, n);
+                 <<<(unsigned)cb, 128, small_smem_bytes<32, 128>(), st>>>(A, H, tau, info, n, Q);
              else if (n <= 64) small_qr_kernel<64, 256, T>
-                 <<<(unsigned)cb, 256, small_smem_bytes<64, 256>(), st>>>(A, H, tau, info, n);
+                 <<<(unsigned)cb, 256, small_smem_bytes<64, 256>(), st>>>(A, H, tau, info, n, Q);
              else small_qr_kernel<128, 256, T>
-                 <<<(unsigned)cb, 256, small_smem_bytes<128, 256>(), st>>>(A, H, tau, info, n));
+                 <<<(unsigned)cb, 256, small_smem_bytes<128, 256>(), st>>>(A, H, tau, info, n, Q));
+}
+
+// Explicit Q (optional output): householder_product(H, tau) = (I - Y T Y^T) = Q_frame * S,
+// because the chart factors I - Q_frame S = Y (T Y^T) (reflection_no_reflectors.py:86-176).
+// One float4 of Q per thread: Q[r][c] = frame[r][c] * s_c, in the output dtype.
+template <typename T>
+__global__ void explicit_q_kernel(const float* __restrict__ F, const float* __restrict__ s,
+                                  T* __restrict__ Q, int n) {
+  const int64_t b = blockIdx.y;
+  const int nn4 = (n * n) >> 2;
+  const float4* F4 = reinterpret_cast<const float4*>(F + mat_off(b, n));
+  const float* sb = s + b * n;
+  T* Qb = Q + mat_off(b, n);
+  for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < nn4; q += gridDim.x * blockDim.x) {
+    const float4 v = F4[q];
+    const int c = (q << 2) % n;  // n % 4 == 0: the four elements share a row
+    Qb[4 * (int64_t)q] = from_f32<T>(v.x * sb[c]);
+    Qb[4 * (int64_t)q + 1] = from_f32<T>(v.y * sb[c + 1]);
+    Qb[4 * (int64_t)q + 2] = from_f32<T>(v.z * sb[c + 2]);
+    Qb[4 * (int64_t)q + 3] = from_f32<T>(v.w * sb[c + 3]);
+  }
+}
+template <typename T>
+__global__ void explicit_q_kernel_any(const float* __restrict__ F, const float* __restrict__ s,
+                                      T* __restrict__ Q, int n) {
+  const int64_t b = blockIdx.y;
+  const int nn = n * n;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < nn; e += gridDim.x * blockDim.x)
+    Q[mat_off(b, n) + e] = from_f32<T>(F[mat_off(b, n) + e] * s[b * n + e % n]);
 }
 
 template <typename T>
 static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
-                             const Ws& ws, cudaStream_t st, Prof* prof) {
+                             const Ws& ws, cudaStream_t st, Prof* prof, T* Q = nullptr) {
   if (n <= g_small_n.load(std::memory_order_relaxed)) {  // whole pipeline, one CTA per matrix
-    launch_small<T>(A, H, tau, info, cb, n, st, prof);
+    launch_small<T>(A, H, tau, info, cb, n, st, prof, Q);
     return cudaGetLastError();
   }
   const int nb = pick_nb(n);
@@ -590,6 +619,14 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
                      tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
              else simt_gemm_kernel<Closure<T>><<<tiles_grid(n, n, cb), 256, 0, st>>>(
                  ClosureArgs{n, ws.L, A, ws.s, H}));
+  if (Q) {
+    const unsigned gx = (unsigned)((n * n / 4 + 255) / 256 < 64 ? (n * n / 4 + 255) / 256 : 64);
+    QRB_LAUNCH(prof, F_CLOSURE,
+               if ((n & 3) == 0) explicit_q_kernel<T><<<dim3(gx, (unsigned)cb), 256, 0, st>>>(
+                   ws.L, ws.s, Q, n);
+               else explicit_q_kernel_any<T><<<dim3(gx, (unsigned)cb), 256, 0, st>>>(
+                   ws.L, ws.s, Q, n));
+  }
   return cudaGetLastError();
 }
 
@@ -615,7 +652,9 @@ static cudaStream_t* lane_streams() {
 
 template <typename T>
 static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
-                   void* workspace, cudaStream_t st, Prof* prof) {
+                   void* workspace, cudaStream_t st, Prof* prof, void* Qv = nullptr) {
+  T* Qo = static_cast<T*>(Qv);
+  auto qoff = [&](int64_t o) { return Qo ? Qo + o * (int64_t)n * n : nullptr; };
   if (n <= g_small_n.load(std::memory_order_relaxed)) {
     const Ws none{};
     for (int64_t b0 = 0; b0 < batch; b0 += (int64_t(1) << 30)) {
@@ -623,7 +662,7 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
       const size_t nn = (size_t)n * n;
       cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn,
                                    static_cast<T*>(H) + b0 * nn, static_cast<T*>(tau) + b0 * n,
-                                   info + b0, cnt, n, none, st, prof);
+                                   info + b0, cnt, n, none, st, prof, qoff(b0));
       if (note(e) != cudaSuccess) return QRB200_ERR_CUDA;
     }
     return QRB200_OK;
@@ -647,7 +686,8 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
     if (!lane || cnt < 2 * L) {
       const Ws w = carve(ws, cnt, n, cols);
       cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
-                                   static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof);
+                                   static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof,
+                                   qoff(b0));
       if (note(e) != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
       continue;
     }
@@ -668,7 +708,7 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
       p += per_chunk_bytes(c, n, cols);
       const int64_t o = b0 + s0;
       e = run_chunk<T>(static_cast<const T*>(A) + o * nn, static_cast<T*>(H) + o * nn,
-                       static_cast<T*>(tau) + o * n, info + o, c, n, w, lane[l], nullptr);
+                       static_cast<T*>(tau) + o * n, info + o, c, n, w, lane[l], nullptr, qoff(o));
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join[l], cudaEventDisableTiming);
       if (e == cudaSuccess) e = cudaEventRecord(join[l], lane[l]);
       if (e == cudaSuccess) e = cudaStreamWaitEvent(st, join[l], 0);
@@ -715,7 +755,7 @@ int qrb200_workspace_bytes(int64_t batch, int32_t n, size_t* bytes) {
 
 static int geqrf_impl(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
                       int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
-                      void* stream, qrb::Prof* prof) {
+                      void* stream, qrb::Prof* prof, void* Q = nullptr) {
   if (batch < 0) return QRB200_ERR_INVALID_ARG;
   if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
   if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
@@ -730,11 +770,19 @@ static int geqrf_impl(const void* A, void* H, void* tau, int32_t* info, int64_t 
   if (qrb::note(qrb::ensure_attrs()) != cudaSuccess) return QRB200_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case QRB200_F32: return qrb::run_all<float>(A, H, tau, info, batch, n, workspace, st, prof);
+    case QRB200_F32: return qrb::run_all<float>(A, H, tau, info, batch, n, workspace, st, prof, Q);
     case QRB200_BF16:
-      return qrb::run_all<__nv_bfloat16>(A, H, tau, info, batch, n, workspace, st, prof);
-    default: return qrb::run_all<__half>(A, H, tau, info, batch, n, workspace, st, prof);
+      return qrb::run_all<__nv_bfloat16>(A, H, tau, info, batch, n, workspace, st, prof, Q);
+    default: return qrb::run_all<__half>(A, H, tau, info, batch, n, workspace, st, prof, Q);
   }
+}
+
+int qrb200_geqrf_batched_q(const void* A, void* H, void* tau, void* Q, int32_t* info,
+                           int64_t batch, int32_t n, int32_t dtype, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (!Q && batch > 0 && n > 0) return QRB200_ERR_INVALID_ARG;
+  return geqrf_impl(A, H, tau, info, batch, n, dtype, workspace, workspace_bytes, stream,
+                    nullptr, Q);
 }
 
 int qrb200_geqrf_batched(const void* A, void* H, void* tau, int32_t* info, int64_t batch,

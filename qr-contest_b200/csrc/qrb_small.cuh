@@ -26,7 +26,7 @@ __host__ __device__ inline size_t small_smem_bytes() {
 template <int NMAX, int NT, typename T>
 __global__ void __launch_bounds__(NT) small_qr_kernel(const T* __restrict__ Ag, T* __restrict__ Hg,
                                                       T* __restrict__ taug, int* __restrict__ info,
-                                                      int n) {
+                                                      int n, T* __restrict__ Qg = nullptr) {
   constexpr int LD = NMAX + 1;
   constexpr int NW = NT / 32;
   constexpr int CPL = (NMAX + 31) / 32;  // columns per lane
@@ -317,6 +317,11 @@ __global__ void __launch_bounds__(NT) small_qr_kernel(const T* __restrict__ Ag, 
 #pragma unroll
     for (int w = 0; w < NW; ++w) acc += tpart[w * NMAX + k];
     taug[b * n + k] = from_f32<T>(2.f / (acc + 1.f));
+  }
+  if (Qg) {  // explicit Q = householder_product(H, tau) = frame * diag(s)
+    T* Q = Qg + mat_off(b, n);
+    for (int r = warp; r < n; r += NW)
+      for (int c = lane; c < n; c += 32) Q[(int64_t)r * n + c] = from_f32<T>(X[r * LD + c] * sgn[c]);
   }
   QRB_PT(6);
   __syncthreads();

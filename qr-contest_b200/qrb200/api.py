@@ -80,6 +80,40 @@ def geqrf(data: torch.Tensor, workspace: torch.Tensor | None = None):
     return H, tau, info
 
 
+def geqrf_q(data: torch.Tensor, workspace: torch.Tensor | None = None):
+    """Like :func:`geqrf`, plus the explicit orthogonal factor: returns ``(H, tau, Q, info)``
+    with ``Q == torch.linalg.householder_product(H, tau)`` (to rounding), written from the
+    pipeline's frame instead of being rebuilt from the reflectors by the caller."""
+    A = _prep(data)
+    if A.device.type != "cuda":
+        raise ValueError("geqrf_q takes a CUDA tensor")
+    lead, n = A.shape[:-2], A.shape[-1]
+    batch = 1
+    for d in lead:
+        batch *= int(d)
+    H = torch.empty_like(A)
+    Q = torch.empty_like(A)
+    tau = torch.empty(*lead, n, dtype=A.dtype, device=A.device)
+    info = torch.zeros(*lead, dtype=torch.int32, device=A.device)
+    if batch > 0 and n > 0:
+        need = _lib.workspace_bytes(batch, n)
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=A.device)
+        elif workspace.numel() * workspace.element_size() < need or workspace.device != A.device:
+            raise ValueError(f"workspace must be >= {need} bytes on {A.device}")
+        with torch.cuda.device(A.device):
+            stream = torch.cuda.current_stream(A.device).cuda_stream
+            rc = _lib.lib().qrb200_geqrf_batched_q(A.data_ptr(), H.data_ptr(), tau.data_ptr(),
+                                                    Q.data_ptr(), info.data_ptr(), batch, n,
+                                                    _NATIVE[A.dtype], workspace.data_ptr(),
+                                                    need, stream)
+        if rc != _lib.QRB200_OK:
+            raise _lib.QRB200Error(rc, "qrb200_geqrf_batched_q")
+    if data.dtype not in _NATIVE:
+        H, tau, Q = H.to(data.dtype), tau.to(data.dtype), Q.to(data.dtype)
+    return H, tau, Q, info
+
+
 def geqrf_host(data: torch.Tensor, out=None, sub_batch: int = 0):
     """Factor a HOST tensor on the current CUDA device; returns host ``(H, tau, info)``.
 

@@ -38,7 +38,15 @@ def load(name):
     return d
 
 
+# At n = 512 the ill-conditioned class (cond(A) = 1e6) is gated only: its frame's trailing
+# columns are determined to about cond(A[:, :k]) * eps32, and tau there differs between two
+# correct float32 implementations by up to 0.7 (measured: this library vs the reference).
+GATE_ONLY = ("illcond_n512",)
+
+
 def kind(name):
+    if name in GATE_ONLY:
+        return "gate"
     if name.startswith("c5_"):
         return "c5"
     if name.startswith("bf16"):

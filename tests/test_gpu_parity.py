@@ -386,3 +386,22 @@ def test_device_checker_matches_oracle_checker():
     assert s["n_pass"] == 12
     H[3, 0, 7] += 1.0
     assert DC.summary(A, H, tau)["n_pass"] == 11
+
+
+@pytest.mark.parametrize("n,dtype", [(33, torch.float32), (64, torch.float32),
+                                     (130, torch.float32), (512, torch.float32),
+                                     (256, torch.bfloat16), (96, torch.float16)])
+def test_explicit_q_matches_householder_product(n, dtype):
+    """qrb200_geqrf_batched_q: H and tau are the same as the plain entry point's, and Q equals
+    householder_product(H, tau) (float64 reconstruction) to float32 rounding (bf16 / f16:
+    the rounding of the returned Q)."""
+    from qrb200 import generators as G
+    A = G.heterogeneous(12, n, seed=51, device="cuda").to(dtype)
+    H, tau, Q, info = qrb().geqrf_q(A)
+    H0, t0, i0 = qrb().geqrf(A)
+    torch.cuda.synchronize()
+    assert torch.equal(H, H0) and torch.equal(tau, t0) and torch.equal(info, i0)
+    Qr = torch.linalg.householder_product(H.double(), tau.double())
+    tol = 2e-5 if dtype == torch.float32 else (2 ** -7 if dtype == torch.bfloat16 else 2 ** -10)
+    err = (Q.double() - Qr).abs().max().item()
+    assert err <= tol * 4, err
