@@ -21,6 +21,7 @@
 #include "qrb_tcx.cuh"
 #include "qrb_tmap.cuh"
 #include "qrb_small.cuh"
+#include "qrb_warp.cuh"
 
 #include <atomic>
 #include <type_traits>
@@ -454,8 +455,9 @@ template <typename T>
 static void launch_small(const T* A, T* H, T* tau, int* info, int64_t cb, int n, cudaStream_t st,
                          Prof* prof, T* Q) {
   QRB_LAUNCH(prof, F_SMALL,
-             if (n <= 32) small_qr_kernel<32, 128, T>
-                 <<<(unsigned)cb, 128, small_smem_bytes<32, 128>(), st>>>(A, H, tau, info, n, Q);
+             if (n <= kWarpMaxN) warp_qr_kernel<T>
+                 <<<(unsigned)((cb + kWarpWPB - 1) / kWarpWPB), 32 * kWarpWPB, 0, st>>>(
+                     A, H, tau, info, n, cb, Q);
              else if (n <= 64) small_qr_kernel<64, 256, T>
                  <<<(unsigned)cb, 256, small_smem_bytes<64, 256>(), st>>>(A, H, tau, info, n, Q);
              else small_qr_kernel<128, 256, T>

@@ -405,3 +405,18 @@ def test_explicit_q_matches_householder_product(n, dtype):
     tol = 2e-5 if dtype == torch.float32 else (2 ** -7 if dtype == torch.bfloat16 else 2 ** -10)
     err = (Q.double() - Qr).abs().max().item()
     assert err <= tol * 4, err
+
+
+@pytest.mark.parametrize("n,b", [(1, 5), (7, 9), (20, 13), (32, 6), (32, 4099)])
+def test_warp_kernel_classes_vs_oracle(n, b):
+    """n <= 32 runs one warp per matrix (four matrices per CTA; batches that do not fill the
+    last CTA included): all six classes gated, dense matrices elementwise against the oracle,
+    and identical results for the same matrix wherever it sits in the batch."""
+    from qrb200 import generators as G
+    A = G.heterogeneous(max(b, 6), n, seed=61, layout="roundrobin", device="cpu")[:b]
+    H, tau = run(A)
+    assert_gates(A, H, tau, f"warp n={n}")
+    Ho, to = O.custom_kernel_np(A[:6].numpy())
+    assert_tight(H[0], tau[0], Ho[0], to[0])
+    H1, t1 = run(A[1:2].clone())
+    assert torch.equal(H1[0], H[1]) and torch.equal(t1[0], tau[1])
