@@ -82,6 +82,22 @@ int qrb200_geqrf_batched_q(const void* A, void* H, void* tau, void* Q, int32_t* 
                            int64_t batch, int32_t n, int32_t dtype, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* Batched QR of `batch` tall row-major m x n matrices (m >= n; m == n is the square call).
+ *   A     [batch][m][n]  input, element type `dtype`
+ *   H     [batch][m][n]  output: s_i R_ij on and above the diagonal of the top n x n block,
+ *                        the n reflector tails below it (torch.geqrf's layout for m x n)
+ *   tau   [batch][n]     output;  info [batch] as for qrb200_geqrf_batched (the
+ *                        informational QRB200_INFO_LU_ZERO_PIVOT bit is not reported)
+ * Replaces the reference's rectangular chart modlu_rect (irregular/exp1_irregular.py:106-122:
+ * the unpivoted sign-rule elimination over the n columns of an m x n frame), here applied to
+ * the frame of reflection_no_reflectors.py:55-81 computed from the tall A itself.  Every
+ * stage is column-nested, so the square kernels run on [A | 0] (m x m) with the CholeskyQR
+ * jitter averaged over the first n diagonal entries, and the first n columns are returned:
+ * the cost is that of an m x m factorization.  Padded buffers are allocated stream-ordered
+ * (cudaMallocAsync) per call. */
+int qrb200_geqrf_batched_rect(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
+                              int32_t m, int32_t n, int32_t dtype, void* stream);
+
 /* Same computation as qrb200_geqrf_batched, with every kernel launch bracketed by CUDA
  * events on `stream`; blocks until the stream is idle and writes the summed device time
  * (milliseconds) of each kernel family into family_ms[0 .. qrb200_num_families()-1].

@@ -37,7 +37,8 @@ def _bmm(a, b):
 # Stage I-a: partial-pivot LU  (reflection_no_reflectors.py:66, torch.linalg.lu -> getrf)
 # --------------------------------------------------------------------------------------
 def lu_partial_pivot(A, nb: int = 32):
-    """Blocked right-looking LU with partial pivoting of a batch ``A (b,n,n)``.
+    """Blocked right-looking LU with partial pivoting of a batch ``A (b,m,n)``, m >= n
+    (square for the reference entry point; tall for the rectangular variant).
 
     Returns ``(LU, perm)``: ``LU`` packs the unit-lower ``L`` (strictly below the
     diagonal) and ``U``; ``perm[b, j]`` is the row of ``A`` that became row ``j`` of
@@ -45,8 +46,8 @@ def lu_partial_pivot(A, nb: int = 32):
     ``P`` that ``torch.linalg.lu`` returns).
     """
     A = np.array(A, dtype=F32, copy=True)
-    b, n, _ = A.shape
-    perm = np.tile(np.arange(n), (b, 1))
+    b, m, n = A.shape
+    perm = np.tile(np.arange(m), (b, 1))
     bi = np.arange(b)
     for k0 in range(0, n, nb):
         k1 = min(k0 + nb, n)
@@ -77,7 +78,7 @@ def lu_partial_pivot(A, nb: int = 32):
 
 
 def unit_lower(LU):
-    n = LU.shape[-1]
+    n = LU.shape[-1]           # m x n: unit lower trapezoidal
     L = np.tril(LU, -1)
     L[:, np.arange(n), np.arange(n)] = 1.0
     return L.astype(F32)
@@ -147,7 +148,7 @@ def frame(A):
     L = unit_lower(LU)
     Q1, ok1 = cholqr_pass(L)
     Q, ok2 = cholqr_pass(Q1)
-    b, n, _ = Q.shape
+    b = Q.shape[0]
     PQ = np.empty_like(Q)
     PQ[np.arange(b)[:, None], perm, :] = Q          # (P Q)[perm[j]] = Q[j]
     return PQ, perm, ok1 & ok2
@@ -164,7 +165,7 @@ def chart(Q, bs: int = 32):
     multipliers ``Y[i,k] = -s_k M[i,k] / piv`` (:158).  Blocked exactly as :144-174.
     """
     M = np.array(Q, dtype=F32, copy=True)
-    b, n, _ = M.shape
+    b, m, n = M.shape          # m > n: the rectangular chart (irregular/exp1_irregular.py:106-122)
     Y = np.zeros_like(M)
     s = np.ones((b, n), dtype=F32)
     for k0 in range(0, n, bs):
@@ -177,7 +178,7 @@ def chart(Q, bs: int = 32):
             sk = np.where(take_plus, F32(1.0), F32(-1.0)).astype(F32)
             piv = np.where(take_plus, pp, pm).astype(F32)
             s[:, k] = sk
-            if k + 1 < n:
+            if k + 1 < m:
                 mult = (-sk[:, None] * M[:, k + 1:, k]) / piv[:, None]
                 Y[:, k + 1:, k] = mult
                 if k + 1 < k1:
@@ -212,6 +213,24 @@ def custom_kernel_np(A, return_info: bool = False):
     if return_info:
         return H, tau, (~ok).astype(np.int32) if A3.shape[0] else np.zeros(0, np.int32)
     return H, tau
+
+
+def custom_kernel_rect_np(A):
+    """Tall ``A (b, m, n)``, m >= n -> ``(H (b, m, n), tau (b, n))``: the same frame, closure and
+    chart on an m x n input.  The LU pivots over m rows, CholeskyQR2 runs on the m x n unit
+    lower-trapezoidal L (jitter over its n Gram diagonal entries), the closure is the n x n
+    triu(Q^T A), and the chart is the reference's rectangular elimination over the n columns
+    of the frame (modlu_rect, irregular/exp1_irregular.py:106-122) with the sign rule of
+    reflection_no_reflectors.py:149-158."""
+    A3 = np.asarray(A, dtype=F32)
+    b, m, n = A3.shape
+    Q, _perm, _ok = frame(A3)
+    R = np.triu(_bmm(np.swapaxes(Q, 1, 2), A3))
+    Y, s = chart(Q)
+    tau = (F32(2.0) / (np.sum(np.square(np.tril(Y, -1)), axis=1) + F32(1.0))).astype(F32)
+    H = np.tril(Y, -1)
+    H[:, :n, :] += np.triu(s[:, :, None] * R)
+    return H.astype(F32), tau
 
 
 def custom_kernel(data):

@@ -359,7 +359,7 @@ static void launch_panel(const PanelArgs& pa, int64_t cb, cudaStream_t st) {
 // tau_k = 2/(1+|y_k|^2) when d_k ~ 0), so its Gram diagonal is recomputed in exact float32
 // column sums.  G lives in ws.T0; R (upper) and L_G^{-1} (strict lower) share ws.R.
 static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, const Ws& ws,
-                        int* info, int info_bit, cudaStream_t st, Prof* prof) {
+                        int* info, int info_bit, cudaStream_t st, Prof* prof, int nmu) {
   const bool tcp = use_tc(n);
   const bool rw = use_rankw(n);
   const bool pass2 = (info_bit == INFO_CHOL2_NOT_PD);
@@ -397,7 +397,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
       PanelArgs pa{};
       pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = ldw;
       pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = Wp; pa.Wc = Wcp; pa.Bp = Bpp;
-      pa.mu = ws.mu; pa.info = info; pa.info_bit = info_bit;
+      pa.mu = ws.mu; pa.nmu = nmu; pa.info = info; pa.info_bit = info_bit;
       QRB_LAUNCH(prof, F_CHOL_PANEL,
                  (launch_panel<PM_CHOL, float, float>(pa, cb, st)));
       const int k1 = k0 + w;
@@ -453,15 +453,15 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
 
 template <typename T>
 static void launch_small(const T* A, T* H, T* tau, int* info, int64_t cb, int n, cudaStream_t st,
-                         Prof* prof, T* Q) {
+                         Prof* prof, T* Q, int nmu) {
   QRB_LAUNCH(prof, F_SMALL,
              if (n <= kWarpMaxN) warp_qr_kernel<T>
                  <<<(unsigned)((cb + kWarpWPB - 1) / kWarpWPB), 32 * kWarpWPB, 0, st>>>(
-                     A, H, tau, info, n, cb, Q);
+                     A, H, tau, info, n, cb, Q, nmu > 0 ? nmu : n);
              else if (n <= 64) small_qr_kernel<64, 256, T>
-                 <<<(unsigned)cb, 256, small_smem_bytes<64, 256>(), st>>>(A, H, tau, info, n, Q);
+                 <<<(unsigned)cb, 256, small_smem_bytes<64, 256>(), st>>>(A, H, tau, info, n, Q, nmu);
              else small_qr_kernel<128, 256, T>
-                 <<<(unsigned)cb, 256, small_smem_bytes<128, 256>(), st>>>(A, H, tau, info, n, Q));
+                 <<<(unsigned)cb, 256, small_smem_bytes<128, 256>(), st>>>(A, H, tau, info, n, Q, nmu));
 }
 
 // Explicit Q (optional output): householder_product(H, tau) = (I - Y T Y^T) = Q_frame * S,
@@ -495,9 +495,10 @@ __global__ void explicit_q_kernel_any(const float* __restrict__ F, const float* 
 
 template <typename T>
 static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
-                             const Ws& ws, cudaStream_t st, Prof* prof, T* Q = nullptr) {
+                             const Ws& ws, cudaStream_t st, Prof* prof, T* Q = nullptr,
+                             int nmu = 0) {
   if (n <= g_small_n.load(std::memory_order_relaxed)) {  // whole pipeline, one CTA per matrix
-    launch_small<T>(A, H, tau, info, cb, n, st, prof, Q);
+    launch_small<T>(A, H, tau, info, cb, n, st, prof, Q, nmu);
     return cudaGetLastError();
   }
   const int nb = pick_nb(n);
@@ -550,8 +551,8 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
     }
   }
   // ---- I-b..d: CholeskyQR2 on P*L; the frame Q = P Q_L lands in ws.L ----
-  cholqr_pass(ws.L, ws.Q1, n, cb, nb, ws, info, INFO_CHOL1_NOT_PD, st, prof);
-  cholqr_pass(ws.Q1, ws.L, n, cb, nb, ws, info, INFO_CHOL2_NOT_PD, st, prof);
+  cholqr_pass(ws.L, ws.Q1, n, cb, nb, ws, info, INFO_CHOL1_NOT_PD, st, prof, nmu);
+  cholqr_pass(ws.Q1, ws.L, n, cb, nb, ws, info, INFO_CHOL2_NOT_PD, st, prof, nmu);
 
   // ---- III: chart on a copy of Q (working copy in ws.T0) ----
   // The chart's trailing updates stay on float32 FMA tiles: tau_k = 2/(1+|y_k|^2) sits at 1
@@ -654,7 +655,8 @@ static cudaStream_t* lane_streams() {
 
 template <typename T>
 static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t batch, int n,
-                   void* workspace, cudaStream_t st, Prof* prof, void* Qv = nullptr) {
+                   void* workspace, cudaStream_t st, Prof* prof, void* Qv = nullptr,
+                   int nmu = 0) {
   T* Qo = static_cast<T*>(Qv);
   auto qoff = [&](int64_t o) { return Qo ? Qo + o * (int64_t)n * n : nullptr; };
   if (n <= g_small_n.load(std::memory_order_relaxed)) {
@@ -664,7 +666,7 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
       const size_t nn = (size_t)n * n;
       cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn,
                                    static_cast<T*>(H) + b0 * nn, static_cast<T*>(tau) + b0 * n,
-                                   info + b0, cnt, n, none, st, prof, qoff(b0));
+                                   info + b0, cnt, n, none, st, prof, qoff(b0), nmu);
       if (note(e) != cudaSuccess) return QRB200_ERR_CUDA;
     }
     return QRB200_OK;
@@ -689,7 +691,7 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
       const Ws w = carve(ws, cnt, n, cols);
       cudaError_t e = run_chunk<T>(static_cast<const T*>(A) + b0 * nn, static_cast<T*>(H) + b0 * nn,
                                    static_cast<T*>(tau) + b0 * n, info + b0, cnt, n, w, st, prof,
-                                   qoff(b0));
+                                   qoff(b0), nmu);
       if (note(e) != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
       continue;
     }
@@ -710,7 +712,8 @@ static int run_all(const void* A, void* H, void* tau, int32_t* info, int64_t bat
       p += per_chunk_bytes(c, n, cols);
       const int64_t o = b0 + s0;
       e = run_chunk<T>(static_cast<const T*>(A) + o * nn, static_cast<T*>(H) + o * nn,
-                       static_cast<T*>(tau) + o * n, info + o, c, n, w, lane[l], nullptr, qoff(o));
+                       static_cast<T*>(tau) + o * n, info + o, c, n, w, lane[l], nullptr, qoff(o),
+                       nmu);
       if (e == cudaSuccess) e = cudaEventCreateWithFlags(&join[l], cudaEventDisableTiming);
       if (e == cudaSuccess) e = cudaEventRecord(join[l], lane[l]);
       if (e == cudaSuccess) e = cudaStreamWaitEvent(st, join[l], 0);
@@ -757,7 +760,7 @@ int qrb200_workspace_bytes(int64_t batch, int32_t n, size_t* bytes) {
 
 static int geqrf_impl(const void* A, void* H, void* tau, int32_t* info, int64_t batch,
                       int32_t n, int32_t dtype, void* workspace, size_t workspace_bytes,
-                      void* stream, qrb::Prof* prof, void* Q = nullptr) {
+                      void* stream, qrb::Prof* prof, void* Q = nullptr, int nmu = 0) {
   if (batch < 0) return QRB200_ERR_INVALID_ARG;
   if (n < 0 || n > qrb::kMaxN) return QRB200_ERR_UNSUPPORTED_N;
   if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
@@ -772,10 +775,11 @@ static int geqrf_impl(const void* A, void* H, void* tau, int32_t* info, int64_t 
   if (qrb::note(qrb::ensure_attrs()) != cudaSuccess) return QRB200_ERR_CUDA;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case QRB200_F32: return qrb::run_all<float>(A, H, tau, info, batch, n, workspace, st, prof, Q);
+    case QRB200_F32:
+      return qrb::run_all<float>(A, H, tau, info, batch, n, workspace, st, prof, Q, nmu);
     case QRB200_BF16:
-      return qrb::run_all<__nv_bfloat16>(A, H, tau, info, batch, n, workspace, st, prof, Q);
-    default: return qrb::run_all<__half>(A, H, tau, info, batch, n, workspace, st, prof, Q);
+      return qrb::run_all<__nv_bfloat16>(A, H, tau, info, batch, n, workspace, st, prof, Q, nmu);
+    default: return qrb::run_all<__half>(A, H, tau, info, batch, n, workspace, st, prof, Q, nmu);
   }
 }
 
@@ -1088,4 +1092,108 @@ extern "C" int qrb200_release_host_staging(void) {
   hs.base = nullptr;
   hs.bytes = 0;
   return QRB200_OK;
+}
+
+// ---------------------------------------------------------------------------------------
+// Rectangular (tall) entry point.
+//
+// The pipeline is column-nested: the LU's pivot choices and L's first n columns, the
+// Cholesky factor's leading n x n block, the frame's first n columns, the chart's first n
+// multipliers, signs and tau, and the closure's first n columns all depend only on A's first
+// n columns.  So a tall m x n matrix is factored by the square kernels on the m x m matrix
+// [A | 0], with the CholeskyQR jitter's mean taken over the first n diagonal entries only
+// (the one quantity that would see the padding), and the first n columns of H and tau are
+// returned.  On the zero columns the LU meets zero pivots, which leave L unit lower
+// triangular, so the padded frame stays well defined.
+// ---------------------------------------------------------------------------------------
+namespace qrb {
+
+template <typename E>  // E: an element-sized integer (the copy never converts)
+__global__ void pad_cols_kernel(const E* __restrict__ A, E* __restrict__ P, int m, int n) {
+  const int64_t b = blockIdx.y;
+  const int64_t mm = (int64_t)m * m;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < mm;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / m), c = (int)(e - (int64_t)r * m);
+    P[b * mm + e] = (c < n) ? A[b * (int64_t)m * n + (int64_t)r * n + c] : E(0);
+  }
+}
+
+template <typename E>
+__global__ void crop_cols_kernel(const E* __restrict__ P, const E* __restrict__ tp,
+                                 E* __restrict__ H, E* __restrict__ tau, int* __restrict__ info,
+                                 int m, int n) {
+  const int64_t b = blockIdx.y;
+  const int64_t mn = (int64_t)m * n;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < mn;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int r = (int)(e / n), c = (int)(e - (int64_t)r * n);
+    H[b * mn + e] = P[b * (int64_t)m * m + (int64_t)r * m + c];
+  }
+  if (blockIdx.x == 0) {
+    for (int k = threadIdx.x; k < n; k += blockDim.x) tau[b * n + k] = tp[b * m + k];
+    // zero pivots are expected on the padding columns: the informational bit is not reported
+    if (threadIdx.x == 0) info[b] &= ~INFO_LU_ZERO_PIVOT;
+  }
+}
+
+constexpr size_t kRectBudget = size_t(8) << 30;  // padded A, H, tau per chunk
+
+}  // namespace qrb
+
+extern "C" int qrb200_geqrf_batched_rect(const void* A, void* H, void* tau, int32_t* info,
+                                         int64_t batch, int32_t m, int32_t n, int32_t dtype,
+                                         void* stream) {
+  using namespace qrb;
+  if (batch < 0) return QRB200_ERR_INVALID_ARG;
+  if (m < 0 || m > kMaxN || n < 0) return QRB200_ERR_UNSUPPORTED_N;
+  if (n > m) return QRB200_ERR_INVALID_ARG;  // tall or square only
+  if (dtype != QRB200_F32 && dtype != QRB200_BF16 && dtype != QRB200_F16)
+    return QRB200_ERR_INVALID_ARG;
+  if (batch == 0 || n == 0) return QRB200_OK;
+  if (!A || !H || !tau || !info) return QRB200_ERR_INVALID_ARG;
+  if (n == m)
+    return geqrf_impl(A, H, tau, info, batch, n, dtype, nullptr, 0, stream, nullptr);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t es = dtype == QRB200_F32 ? 4 : 2;
+  const size_t mm = (size_t)m * m;
+  const size_t per = 2 * mm * es + m * es + 3 * 256;
+  int64_t cb = (int64_t)(kRectBudget / per);
+  if (cb < 1) cb = 1;
+  if (cb > kMaxChunk) cb = kMaxChunk;
+  if (cb > batch) cb = batch;
+  const size_t a_b = align256(cb * mm * es), t_b = align256(cb * m * es);
+  void* buf = nullptr;
+  if (note(cudaMallocAsync(&buf, 2 * a_b + t_b, st)) != cudaSuccess) return QRB200_ERR_CUDA;
+  char* Ap = static_cast<char*>(buf);
+  char* Hp = Ap + a_b;
+  char* Tp = Hp + a_b;
+  int rc = QRB200_OK;
+  for (int64_t b0 = 0; b0 < batch && rc == QRB200_OK; b0 += cb) {
+    const int64_t cnt = batch - b0 < cb ? batch - b0 : cb;
+    const dim3 pg((unsigned)((mm + 255) / 256 < 128 ? (mm + 255) / 256 : 128), (unsigned)cnt);
+    const dim3 cg((unsigned)(((size_t)m * n + 255) / 256 < 128 ? ((size_t)m * n + 255) / 256 : 128),
+                  (unsigned)cnt);
+    const char* Ab = static_cast<const char*>(A) + b0 * (int64_t)m * n * es;
+    if (es == 4)
+      pad_cols_kernel<uint32_t><<<pg, 256, 0, st>>>((const uint32_t*)Ab, (uint32_t*)Ap, m, n);
+    else
+      pad_cols_kernel<uint16_t><<<pg, 256, 0, st>>>((const uint16_t*)Ab, (uint16_t*)Ap, m, n);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (note(cudaGetLastError()) != cudaSuccess) { rc = QRB200_ERR_CUDA; break; }
+    rc = geqrf_impl(Ap, Hp, Tp, info + b0, cnt, m, dtype, nullptr, 0, stream, nullptr, nullptr, n);
+    if (rc != QRB200_OK) break;
+    char* Hb = static_cast<char*>(H) + b0 * (int64_t)m * n * es;
+    char* tb = static_cast<char*>(tau) + b0 * (int64_t)n * es;
+    if (es == 4)
+      crop_cols_kernel<uint32_t><<<cg, 256, 0, st>>>((const uint32_t*)Hp, (const uint32_t*)Tp,
+                                                     (uint32_t*)Hb, (uint32_t*)tb, info + b0, m, n);
+    else
+      crop_cols_kernel<uint16_t><<<cg, 256, 0, st>>>((const uint16_t*)Hp, (const uint16_t*)Tp,
+                                                     (uint16_t*)Hb, (uint16_t*)tb, info + b0, m, n);
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    if (note(cudaGetLastError()) != cudaSuccess) rc = QRB200_ERR_CUDA;
+  }
+  if (note(cudaFreeAsync(buf, st)) != cudaSuccess && rc == QRB200_OK) rc = QRB200_ERR_CUDA;
+  return rc;
 }

@@ -55,6 +55,8 @@ struct PanelArgs {
   float* Bp;         // CHOL: [b][ldw][n] out, rows of L_G^{-1} [k0, k0+w) before the panel
                      //       (columns < k0+w, identity block included)
   float* mu;         // CHOL: [b] jitter, computed when k0 == 0
+  int nmu;           // CHOL: diagonal entries in the jitter's mean (0 = n; the rectangular
+                     //       entry point's zero-padded columns are left out of it)
   void* H;           // CHART: [b][n][n] out (output dtype), strict lower part
   void* tau;         // CHART: [b][n] out (output dtype)
   float* s;          // CHART: [b][n] out, signs
@@ -95,14 +97,14 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
   if (MODE == PM_CHOL) {
     if (k0 == 0) {
       float acc = 0.f;
-      for (int i = tid; i < n; i += 256) acc += to_f32(src[(int64_t)i * n + i]);
+      for (int i = tid; i < (a.nmu > 0 ? a.nmu : n); i += 256) acc += to_f32(src[(int64_t)i * n + i]);
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
       if (lane == 0) red_x[warp] = acc;
       __syncthreads();
       if (tid == 0) {
         float t = 0.f;
         for (int i = 0; i < 8; ++i) t += red_x[i];
-        s_mu = 1e-7f * (t / (float)n);
+        s_mu = 1e-7f * (t / (float)(a.nmu > 0 ? a.nmu : n));
         a.mu[b] = s_mu;
       }
     } else if (tid == 0) {

@@ -92,14 +92,14 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   if (MODE == PM_CHOL) {
     if (k0 == 0) {
       float acc = 0.f;
-      for (int i = tid; i < n; i += 256) acc += to_f32(src[(int64_t)i * n + i]);
+      for (int i = tid; i < (a.nmu > 0 ? a.nmu : n); i += 256) acc += to_f32(src[(int64_t)i * n + i]);
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
       if (lane == 0) red_v[0][warp] = acc;
       __syncthreads();
       if (tid == 0) {
         float t = 0.f;
         for (int i = 0; i < 8; ++i) t += red_v[0][i];
-        s_mu = 1e-7f * (t / (float)n);
+        s_mu = 1e-7f * (t / (float)(a.nmu > 0 ? a.nmu : n));
         a.mu[b] = s_mu;
       }
     } else if (tid == 0) {

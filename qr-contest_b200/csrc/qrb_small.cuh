@@ -26,7 +26,8 @@ __host__ __device__ inline size_t small_smem_bytes() {
 template <int NMAX, int NT, typename T>
 __global__ void __launch_bounds__(NT) small_qr_kernel(const T* __restrict__ Ag, T* __restrict__ Hg,
                                                       T* __restrict__ taug, int* __restrict__ info,
-                                                      int n, T* __restrict__ Qg = nullptr) {
+                                                      int n, T* __restrict__ Qg = nullptr,
+                                                      int nmu = 0) {
   constexpr int LD = NMAX + 1;
   constexpr int NW = NT / 32;
   constexpr int CPL = (NMAX + 31) / 32;  // columns per lane
@@ -167,10 +168,11 @@ __global__ void __launch_bounds__(NT) small_qr_kernel(const T* __restrict__ Ag, 
     if (pass == 0) QRB_PT(2);
     if (warp == 0) {  // mu = 1e-7 mean(diag G)  (:74)
       float acc = 0.f;
-      for (int i = lane; i < n; i += 32) acc += G[i * LD + i];
+      const int nm = nmu > 0 ? nmu : n;  // the rectangular entry point's padding is left out
+      for (int i = lane; i < nm; i += 32) acc += G[i * LD + i];
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
-      if (lane == 0) s_f = 1e-7f * (acc / (float)n);
+      if (lane == 0) s_f = 1e-7f * (acc / (float)nm);
     }
     __syncthreads();
     // Cholesky (potf2, right-looking on the lower triangle): column k of G becomes R[k][k..]

@@ -35,7 +35,8 @@ constexpr int kWarpTile = kWarpMaxN * kWarpLD;
 template <typename T>
 __global__ void __launch_bounds__(32 * kWarpWPB)
     warp_qr_kernel(const T* __restrict__ Ag, T* __restrict__ Hg, T* __restrict__ taug,
-                   int* __restrict__ info, int n, int64_t batch, T* __restrict__ Qg) {
+                   int* __restrict__ info, int n, int64_t batch, T* __restrict__ Qg,
+                   int nmu) {
   constexpr int N = kWarpMaxN, LD = kWarpLD;
   constexpr unsigned FULL = 0xffffffffu;
   __shared__ float tiles[kWarpWPB][2][kWarpTile];
@@ -112,14 +113,15 @@ __global__ void __launch_bounds__(32 * kWarpWPB)
       for (int c = 0; c < N; ++c)
         if (c <= lane) g[c] = fmaf(xi, S0[r * LD + c], g[c]);
     }
-    // mu = 1e-7 mean(diag G)  (:74)
+    // mu = 1e-7 mean(diag G) (:74) over the first nmu diagonal entries (all n unless the
+    // rectangular entry point padded the matrix with zero columns)
     float dsum = 0.f;
 #pragma unroll
     for (int c = 0; c < N; ++c)
-      if (c == lane && act) dsum = g[c];
+      if (c == lane && lane < nmu) dsum = g[c];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) dsum += __shfl_down_sync(FULL, dsum, o);
-    const float mu = 1e-7f * (__shfl_sync(FULL, dsum, 0) / (float)n);
+    const float mu = 1e-7f * (__shfl_sync(FULL, dsum, 0) / (float)nmu);
     // right-looking Cholesky on the lower triangle: after step k, lane i > k holds
     // R[k][i] in g[k]; the diagonal's reciprocal goes to rinv_own of lane k
     float rinv_own = 0.f;

@@ -8,7 +8,7 @@ same signature, same output layout (torch.geqrf compact form), same dtype semant
 same error on a Gram that is not positive definite.  The compute path is the CUDA library
 ``libqrb200.so`` (C ABI in ``include/qrb200.h``); there is no CPU fallback.
 """
-from .api import custom_kernel, geqrf, geqrf_q, LinAlgError  # noqa: F401
+from .api import custom_kernel, geqrf, geqrf_q, geqrf_rect, LinAlgError  # noqa: F401
 from . import api  # noqa: F401
 
-__all__ = ["custom_kernel", "geqrf", "geqrf_q", "LinAlgError"]
+__all__ = ["custom_kernel", "geqrf", "geqrf_q", "geqrf_rect", "LinAlgError"]

@@ -51,6 +51,10 @@ SIGNATURES = {
                                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                               ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p,
                                               ctypes.c_size_t, ctypes.c_void_p]),
+    "qrb200_geqrf_batched_rect": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
+                                                 ctypes.c_void_p, ctypes.c_void_p,
+                                                 ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                                 ctypes.c_int32, ctypes.c_void_p]),
     "qrb200_geqrf_batched_timed": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p,
                                                   ctypes.c_void_p, ctypes.c_void_p,
                                                   ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,

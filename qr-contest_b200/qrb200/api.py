@@ -114,6 +114,38 @@ def geqrf_q(data: torch.Tensor, workspace: torch.Tensor | None = None):
     return H, tau, Q, info
 
 
+def geqrf_rect(data: torch.Tensor):
+    """QR of a batch of tall ``(..., m, n)`` CUDA matrices (``m >= n``): returns
+    ``(H, tau, info)`` with ``H (..., m, n)`` and ``tau (..., n)`` in the torch.geqrf layout,
+    ``householder_product(H, tau)`` the ``m x n`` orthonormal factor.  Asynchronous."""
+    if not isinstance(data, torch.Tensor) or data.dim() < 2:
+        raise ValueError("expected a (..., m, n) tensor")
+    m, n = data.shape[-2], data.shape[-1]
+    if n > m:
+        raise ValueError(f"geqrf_rect takes tall or square matrices (got {m} x {n})")
+    if data.device.type != "cuda":
+        raise ValueError("geqrf_rect takes a CUDA tensor")
+    A = (data if data.dtype in _NATIVE else data.to(torch.float32)).contiguous()
+    lead = A.shape[:-2]
+    batch = 1
+    for d in lead:
+        batch *= int(d)
+    H = torch.empty_like(A)
+    tau = torch.empty(*lead, n, dtype=A.dtype, device=A.device)
+    info = torch.zeros(*lead, dtype=torch.int32, device=A.device)
+    if batch > 0 and n > 0:
+        with torch.cuda.device(A.device):
+            stream = torch.cuda.current_stream(A.device).cuda_stream
+            rc = _lib.lib().qrb200_geqrf_batched_rect(A.data_ptr(), H.data_ptr(), tau.data_ptr(),
+                                                       info.data_ptr(), batch, m, n,
+                                                       _NATIVE[A.dtype], stream)
+        if rc != _lib.QRB200_OK:
+            raise _lib.QRB200Error(rc, "qrb200_geqrf_batched_rect")
+    if data.dtype not in _NATIVE:
+        H, tau = H.to(data.dtype), tau.to(data.dtype)
+    return H, tau, info
+
+
 def geqrf_host(data: torch.Tensor, out=None, sub_batch: int = 0):
     """Factor a HOST tensor on the current CUDA device; returns host ``(H, tau, info)``.
 

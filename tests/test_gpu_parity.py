@@ -420,3 +420,51 @@ def test_warp_kernel_classes_vs_oracle(n, b):
     assert_tight(H[0], tau[0], Ho[0], to[0])
     H1, t1 = run(A[1:2].clone())
     assert torch.equal(H1[0], H[1]) and torch.equal(t1[0], tau[1])
+
+
+def rect_gates(A, H, tau):
+    """fp64 gates of a tall factorization: ||R - Q^T A||_1/||A||_1 < 20 m eps32 and
+    ||Q^T Q - I||_1 < 100 m eps32 with Q = householder_product(H, tau) (m x n)."""
+    m, n = A.shape[-2], A.shape[-1]
+    Ad, Hd, td = A.double(), H.double(), tau.double()
+    Q = torch.linalg.householder_product(Hd, td)
+    R = torch.triu(Hd[..., :n, :])
+    f = torch.linalg.matrix_norm(R - Q.mT @ Ad, ord=1) / torch.linalg.matrix_norm(Ad, ord=1)
+    o = torch.linalg.matrix_norm(Q.mT @ Q - torch.eye(n, dtype=torch.float64, device=A.device),
+                                 ord=1)
+    eps = torch.finfo(torch.float32).eps
+    assert bool((f < 20 * m * eps).all()) and bool((o < 100 * m * eps).all()), (f.max(), o.max())
+    assert bool(((td >= 1 - 1e-6) & (td <= 2 + 1e-6)).all())
+
+
+@pytest.mark.parametrize("m,n", [(40, 17), (48, 48), (100, 31), (256, 128), (520, 300),
+                                 (1024, 64)])
+def test_rect_vs_oracle(m, n):
+    """qrb200_geqrf_batched_rect (tall m x n) against the oracle's rectangular restatement:
+    elementwise on dense inputs, gates on all; a square call equals the square entry point."""
+    from qrb200 import generators as G
+    A = G.gaussian((3, m, n), seed=70 + m + n)
+    H, tau, info = qrb().geqrf_rect(A.cuda())
+    torch.cuda.synchronize()
+    assert H.shape == (3, m, n) and tau.shape == (3, n) and int(info.abs().sum()) == 0
+    rect_gates(A.cuda(), H, tau)
+    Ho, to = O.custom_kernel_rect_np(A.numpy())
+    assert_tight(H, tau, Ho, to)
+    if m == n:
+        H0, t0, _ = qrb().geqrf(A.cuda())
+        assert torch.equal(H, H0) and torch.equal(tau, t0)
+
+
+def test_rect_classes_bf16_and_errors():
+    from qrb200 import _lib, generators as G
+    A = G.heterogeneous(12, 160, seed=71, device="cuda")[:, :, :96].contiguous()
+    H, tau, info = qrb().geqrf_rect(A)
+    rect_gates(A, H, tau)
+    Ab = A.to(torch.bfloat16)
+    Hb, tb, _ = qrb().geqrf_rect(Ab)
+    H32, t32, _ = qrb().geqrf_rect(Ab.float())
+    assert torch.equal(Hb, H32.to(torch.bfloat16)) and torch.equal(tb, t32.to(torch.bfloat16))
+    with pytest.raises(ValueError):
+        qrb().geqrf_rect(A.mT.contiguous())
+    rc = _lib.lib().qrb200_geqrf_batched_rect(1, 1, 1, 1, 1, 8, 9, _lib.QRB200_F32, None)
+    assert rc == _lib.QRB200_ERR_INVALID_ARG

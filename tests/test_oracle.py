@@ -126,3 +126,25 @@ def test_checker_flags_bad_factors():
     tau2[:, 3] = 2.5
     _, _, _, _, passed = checker.check(*map(torch.from_numpy, (A, H, tau2)))
     assert not bool(passed.any())
+
+
+def test_rect_oracle_factors_tall_matrices():
+    # the rectangular restatement: Q R = A with Q = householder_product(H, tau) m x n
+    # orthonormal, tau in [1, 2], |diag R| equal to torch.geqrf's; square input = square path
+    rng = np.random.default_rng(6)
+    for m, n in ((50, 20), (64, 64), (33, 1)):
+        A = rng.standard_normal((3, m, n)).astype(np.float32)
+        H, tau = O.custom_kernel_rect_np(A)
+        Hd, td, Ad = (torch.from_numpy(x).double() for x in (H, tau, A))
+        Q = torch.linalg.householder_product(Hd, td)
+        R = torch.triu(Hd[:, :n, :])
+        assert float((Q @ R - Ad).abs().max()) < 1e-4
+        assert float((Q.mT @ Q - torch.eye(n, dtype=torch.float64)).abs().max()) < 1e-5
+        assert ((tau >= 1 - 1e-6) & (tau <= 2 + 1e-6)).all()
+        Hg, _ = torch.geqrf(torch.from_numpy(A))
+        assert torch.allclose(torch.diagonal(R, dim1=-2, dim2=-1).abs().float(),
+                              torch.diagonal(Hg[:, :n, :], dim1=-2, dim2=-1).abs(), atol=1e-4)
+        if m == n:
+            Hs, ts = O.custom_kernel_np(A)
+            np.testing.assert_array_equal(H, Hs)
+            np.testing.assert_array_equal(tau, ts)
