@@ -15,6 +15,7 @@
 #include "qrb_gemm_simt.cuh"
 #include "qrb_panel.cuh"
 #include "qrb_panel_reg.cuh"
+#include "qrb_panel_cl.cuh"
 #include "qrb_tc_ops.cuh"
 #include "qrb_rankw.cuh"
 #include "qrb_tc_rankw.cuh"
@@ -98,7 +99,13 @@ constexpr size_t kPanelSmemCap = 200 * 1024;
 // column block of the two-level Cholesky elimination (QRB200_OPT_CHOL_BLOCK; 0 = one level)
 static std::atomic<int> g_chol_block{128};
 
+// Panels taller than 512 rows run over a CTA cluster (qrb_panel_cl.cuh) when the rows are
+// float4-aligned, up to 4 x 512 rows, so those orders keep 32-wide panels too.
+constexpr int kClusterPanelMaxM = 4 * kClRows;
+static inline bool cluster_panel(int n) { return (n & 3) == 0 && n <= kClusterPanelMaxM; }
+
 static int pick_nb(int n) {
+  if (cluster_panel(n)) return 32;
   for (int w = 32; w >= 8; w >>= 1)
     if (panel_smem_bytes(n, w) <= kPanelSmemCap) return w;
   return 0;
@@ -348,6 +355,10 @@ static void launch_panel(const PanelArgs& pa, int64_t cb, cudaStream_t st) {
   const int m = pa.n - pa.k0;
   if (m <= 256) panel_reg_kernel<MODE, TIn, TOut, 1><<<(unsigned)cb, 256, 0, st>>>(pa);
   else if (m <= 512) panel_reg_kernel<MODE, TIn, TOut, 2><<<(unsigned)cb, 256, 0, st>>>(pa);
+  else if (cluster_panel(pa.n) && m <= 2 * kClRows)
+    panel_cl_kernel<MODE, TIn, TOut, 2><<<(unsigned)(2 * cb), 256, 0, st>>>(pa);
+  else if (cluster_panel(pa.n))
+    panel_cl_kernel<MODE, TIn, TOut, 4><<<(unsigned)(4 * cb), 256, 0, st>>>(pa);
   else panel_kernel<MODE, TIn, TOut><<<(unsigned)cb, 256, panel_smem_bytes(m, pa.w), st>>>(pa);
 }
 
