@@ -161,9 +161,10 @@ const char* qrb200_last_cuda_error(void);
  * allocating library routine.
  *  - Same arguments, results and info bits as qrb200_geqrf_batched (no workspace).
  *  - Returns QRB200_ERR_SCRATCH_LIMIT, before it touches the buffers or the device, when the
- *    working set of a single n x n problem does not fit the scratch: n above 1826 with the
- *    default options (the bound moves with QRB200_OPT_CHOL_BLOCK / QRB200_OPT_CHART_BLOCK,
- *    which size the panel buffers).
+ *    working set of a single n x n problem does not fit the scratch.  With the default options
+ *    that is n above 1792 for n % 4 == 0 (32-wide panels) and above 1826 otherwise (16-wide
+ *    panels); the bound moves with QRB200_OPT_CHOL_BLOCK / QRB200_OPT_CHART_BLOCK, which size
+ *    the panel buffers.
  *  - The first call in each CUDA context of a device (with that device current) looks up the
  *    array's device address; make it before any stream capture.  A device reset creates a
  *    new context and the next call looks the address up again.

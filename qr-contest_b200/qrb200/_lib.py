@@ -19,7 +19,9 @@ QRB200_ERR_CUDA = 4
 QRB200_ERR_SCRATCH_LIMIT = 5
 NOALLOC_SCRATCH_BYTES = 64 << 20
 # largest n the allocation-free entry point accepts with the default block options
+# (n % 4 != 0: 16-wide panels; n % 4 == 0: 32-wide panels, larger panel buffers)
 NOALLOC_MAX_N_DEFAULT = 1826
+NOALLOC_MAX_N4_DEFAULT = 1792
 
 QRB200_F32, QRB200_BF16, QRB200_F16 = 0, 1, 2
 

@@ -144,4 +144,7 @@ def test_noalloc_order_limit_without_gpu():
                                                     _lib.QRB200_F32, None)
     assert call(nmax) == _lib.QRB200_ERR_INVALID_ARG
     assert call(nmax + 1) == _lib.QRB200_ERR_SCRATCH_LIMIT
+    n4 = _lib.NOALLOC_MAX_N4_DEFAULT
+    assert call(n4) == _lib.QRB200_ERR_INVALID_ARG
+    assert call(n4 + 4) == _lib.QRB200_ERR_SCRATCH_LIMIT
     assert call(64) == _lib.QRB200_ERR_INVALID_ARG

@@ -301,9 +301,10 @@ def test_chart_block_widths(block, n):
 
 # ---- the benchmark's own configurations ----
 
-@pytest.mark.parametrize("n", [512, 1024])
+@pytest.mark.parametrize("n", [512, 1024, 1536])
 def test_dense_vs_oracle_large(n):
-    """The measured order and twice it, elementwise against the oracle on dense matrices."""
+    """The measured order and larger ones, elementwise against the oracle on dense matrices
+    (n = 1024 and 1536: panels taller than 512 rows run over 2- and 4-CTA clusters)."""
     g = torch.Generator().manual_seed(2000 + n)
     A = torch.randn(2, n, n, generator=g, dtype=torch.float64).float()
     H, tau = run(A)
