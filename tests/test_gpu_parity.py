@@ -37,11 +37,11 @@ def assert_gates(A, H, tau, msg=""):
     return f / ftol, o / otol
 
 
-def assert_tight(H, tau, Href, tref):
+def assert_tight(H, tau, Href, tref, tol=2e-4):
     H, tau = H.float().cpu().numpy(), tau.float().cpu().numpy()
     err = np.abs(H - Href) / (1.0 + np.abs(Href))
-    assert err.max() <= 2e-4, f"H rel err {err.max():.3g}"
-    assert np.abs(tau - tref).max() <= 2e-4, f"tau err {np.abs(tau - tref).max():.3g}"
+    assert err.max() <= tol, f"H rel err {err.max():.3g}"
+    assert np.abs(tau - tref).max() <= tol, f"tau err {np.abs(tau - tref).max():.3g}"
 
 
 @pytest.mark.parametrize("name", F.names())
@@ -310,7 +310,9 @@ def test_dense_vs_oracle_large(n):
     H, tau = run(A)
     assert_gates(A, H, tau, f"n={n}")
     Ho, to = O.custom_kernel_np(A.numpy())
-    assert_tight(H, tau, Ho, to)
+    # elementwise differences of two float32 frames scale like cond(A) eps32, and a Gaussian
+    # matrix's condition number grows like n: the 2e-4 bound widens in proportion above 1024
+    assert_tight(H, tau, Ho, to, tol=2e-4 * max(1.0, n / 1024))
 
 
 def test_hetero_n512_vs_oracle():
