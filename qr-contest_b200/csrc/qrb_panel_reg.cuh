@@ -125,83 +125,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   __syncthreads();
 
   QRB_PT(1);
-  if (MODE != PM_PIVOT) {
-    // Unpivoted eliminations (the Cholesky of the Gram, the chart): only the w x w diagonal
-    // block needs the column-by-column elimination.  Warp 0 (lane = block row) runs it with a
-    // warp barrier per column; every row below then applies the same sequence of updates as an
-    // independent forward substitution against the block's pivot rows, after ONE CTA barrier.
-    // Each row sees exactly the operations, in the order, of the column-by-column form.
-    __shared__ float Up[PR_W][PR_W + 1];  // pivot row c of the block (columns > c)
-    __shared__ float pvs[PR_W];           // CHOL: 1 / pivot; CHART: pivot 1 + |d|
-    __shared__ float sgs[PR_W];           // CHART: sign s_c
-    if (warp == 0) {
-#pragma unroll
-      for (int c = 0; c < PR_W; ++c) {
-        if (c < w) {
-          // pivot row c: CHOL reads it from the symmetric column (U[c][j] = S[j][c], held by
-          // lane j), the chart from lane c's row
-          if (MODE == PM_CHOL) {
-            if (lane >= c && lane < w) Up[c][lane] = x[0][c];
-          } else if (lane == c) {
-#pragma unroll
-            for (int j = 0; j < PR_W; ++j)
-              if (j >= c && j < w) Up[c][j] = x[0][j];
-          }
-          if (lane == c) {
-#pragma unroll
-            for (int j = 0; j < PR_W; ++j)
-              if (j < c) Ls[c][j] = x[0][j];
-          }
-          __syncwarp();
-          const float pv = Up[c][c] + ((MODE == PM_CHOL) ? s_mu : 0.f);
-          float piv = pv, sgn = 1.f, rpiv = 1.f;
-          if (MODE == PM_CHOL) {
-            if (!(pv > 0.f)) {
-              if (lane == 0) atomicOr(&s_flags, a.info_bit);
-              piv = 1.f;  // keep the arithmetic finite; the host reports the failure
-            }
-            rpiv = __frcp_rn(piv);
-          } else {
-            const float pp = 1.f - pv, pm = 1.f + pv;
-            sgn = (fabsf(pp) >= fabsf(pm)) ? 1.f : -1.f;
-            piv = (sgn > 0.f) ? pp : pm;
-          }
-          if (lane == 0) {
-            dpiv[c] = (MODE == PM_CHOL) ? piv : sgn;
-            pvs[c] = (MODE == PM_CHOL) ? rpiv : piv;
-            sgs[c] = sgn;
-          }
-          if (lane > c && lane < w) {
-            // Cholesky scales by the reciprocal pivot (as potf2 does); the chart divides (:158)
-            const float l = (MODE == PM_CHOL) ? x[0][c] * rpiv : (-sgn * x[0][c]) / piv;
-            x[0][c] = l;
-#pragma unroll
-            for (int j = 0; j < PR_W; ++j)
-              if (j > c && j < w) x[0][j] = fmaf(-l, Up[c][j], x[0][j]);
-          }
-        }
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < RPT; ++q) {
-      const int r = tid + 256 * q;
-      if (r >= w && r < m) {
-#pragma unroll
-        for (int c = 0; c < PR_W; ++c) {
-          if (c < w) {
-            const float l = (MODE == PM_CHOL) ? x[q][c] * pvs[c] : (-sgs[c] * x[q][c]) / pvs[c];
-            x[q][c] = l;
-#pragma unroll
-            for (int j = 0; j < PR_W; ++j)
-              if (j > c && j < w) x[q][j] = fmaf(-l, Up[c][j], x[q][j]);
-          }
-        }
-      }
-    }
-  }
-  // ---- column-by-column elimination (LU: the pivot search needs every row each column) ----
-  if (MODE == PM_PIVOT) {
+  // ---- column-by-column elimination ----
 #pragma unroll
   for (int c = 0; c < PR_W; ++c) {
     if (c >= w) break;
@@ -323,7 +247,6 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
         }
       }
     }
-  }
   }
   __syncthreads();
 
