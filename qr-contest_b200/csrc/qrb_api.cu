@@ -214,8 +214,26 @@ static cudaError_t small_attr() {
 
 template <class Pb>
 static cudaError_t tcx_attr() {
-  return cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              tcx::smem_bytes<Pb>());
+  cudaError_t e = cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb, tcx::CfgWide>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       tcx::smem_bytes<Pb, tcx::CfgWide>());
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb, tcx::CfgDual>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              tcx::smem_bytes<Pb, tcx::CfgDual>());
+}
+
+// TMA-fed tile launch: reductions of K <= 512 run two CTAs per SM (tcx::CfgDual), longer ones
+// the one-CTA shape that drains TMEM into registers (tcx::CfgWide).
+template <class Pb>
+static void launch_tcx(dim3 grid, const tcx::Maps& mp, const typename Pb::Args& args, int K,
+                       cudaStream_t st) {
+  if (K <= tcx::kDualMaxK)
+    tcx::tcx_gemm_kernel<Pb, tcx::CfgDual>
+        <<<grid, tcx::XTHREADS, tcx::smem_bytes<Pb, tcx::CfgDual>(), st>>>(mp, args);
+  else
+    tcx::tcx_gemm_kernel<Pb, tcx::CfgWide>
+        <<<grid, tcx::XTHREADS, tcx::smem_bytes<Pb, tcx::CfgWide>(), st>>>(mp, args);
 }
 
 // TMA maps for a tcx launch: operands stored k-major use 128-row boxes, m-major 32-row boxes.
@@ -377,9 +395,8 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   tcx::Maps gm;
   const bool gx = tcp && tcx_maps(gm, X, false, X, false, n, cb);
   QRB_LAUNCH(prof, F_GRAM,
-             if (gx) tcx::tcx_gemm_kernel<tcx::GramX><<<tc_grid(n, n, cb), tcx::XTHREADS,
-                                                        tcx::smem_bytes<tcx::GramX>(), st>>>(
-                 gm, tc::GramTCArgs{n, X, ws.T0, info});
+             if (gx) launch_tcx<tcx::GramX>(tc_grid(n, n, cb), gm, tc::GramTCArgs{n, X, ws.T0, info},
+                                            n, st);
              else if (tcp) tc::tc_gemm_kernel<tc::GramTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                kTcSmem, st>>>(
                  tc::GramTCArgs{n, X, ws.T0, info});
@@ -440,13 +457,11 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
       const tc::SyrkTCArgs sa{n, kb, ke, ws.T0, ws.R, info};
       const tc::LinvBlkArgs la{n, kb, ke, ldw, ws.R, ws.W, ws.Bp, info};
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 if (sx) tcx::tcx_gemm_kernel<tcx::SyrkX><<<tc_grid(n - ke, n - ke, cb), tcx::XTHREADS,
-                                                             tcx::smem_bytes<tcx::SyrkX>(), st>>>(sm_, sa);
+                 if (sx) launch_tcx<tcx::SyrkX>(tc_grid(n - ke, n - ke, cb), sm_, sa, ke - kb, st);
                  else tc::tc_gemm_kernel<tc::SyrkTC, kTcBN><<<tc_grid(n - ke, n - ke, cb), tc::NTHREADS,
                                                               kTcSmem, st>>>(sa));
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
-                 if (lx) tcx::tcx_gemm_kernel<tcx::LinvBlkX><<<tc_grid(n - ke, ke, cb), tcx::XTHREADS,
-                                                                tcx::smem_bytes<tcx::LinvBlkX>(), st>>>(lm_, la);
+                 if (lx) launch_tcx<tcx::LinvBlkX>(tc_grid(n - ke, ke, cb), lm_, la, ke - kb, st);
                  else tc::tc_gemm_kernel<tc::LinvBlkTC, kTcBN><<<tc_grid(n - ke, ke, cb), tc::NTHREADS,
                                                                 kTcSmem, st>>>(la));
     }
@@ -455,8 +470,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
   tcx::Maps qm;
   const bool qx = tcp && tcx_maps(qm, X, true, ws.R, true, n, cb);
   QRB_LAUNCH(prof, F_QAPPLY,
-             if (qx) tcx::tcx_gemm_kernel<tcx::QApplyX><<<tc_grid(n, n, cb), tcx::XTHREADS,
-                                                          tcx::smem_bytes<tcx::QApplyX>(), st>>>(qm, qa);
+             if (qx) launch_tcx<tcx::QApplyX>(tc_grid(n, n, cb), qm, qa, n, st);
              else if (tcp) tc::tc_gemm_kernel<tc::QApplyTC, kTcBN><<<tc_grid(n, n, cb), tc::NTHREADS,
                                                                 kTcSmem, st>>>(qa);
              else simt_gemm_kernel<QApply><<<tiles_grid(n, n, cb), 256, 0, st>>>(qa));
@@ -625,9 +639,8 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   tcx::Maps cm;
   const bool cx = tcp && std::is_same<T, float>::value && tcx_maps(cm, ws.L, false, A, false, n, cb);
   QRB_LAUNCH(prof, F_CLOSURE,
-             if (cx) tcx::tcx_gemm_kernel<tcx::ClosureX><<<tc_grid(n, n, cb), tcx::XTHREADS,
-                                                           tcx::smem_bytes<tcx::ClosureX>(), st>>>(
-                 cm, tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
+             if (cx) launch_tcx<tcx::ClosureX>(tc_grid(n, n, cb), cm,
+                                               tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info}, n, st);
              else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>
                  <<<tc_grid(n, n, cb), tc::NTHREADS, kTcSmem, st>>>(
                      tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});

@@ -39,9 +39,24 @@ constexpr int PLANE_SETS = 2;      // split of stage t+1 overlaps the MMAs of st
 // A_TMEM policies keep A in tensor memory: a plane set holds B hi / lo only.
 template <bool A_TMEM>
 constexpr int plane_set_bytes() { return (A_TMEM ? 2 : 4) * PLANE; }
-template <class Pb>
+// Pipeline shape of a launch: RS raw stages, PS plane / TMEM-operand sets, LONGK = drain the
+// TMEM accumulator into float32 registers in long reductions, MINB = CTAs per SM it is built for.
+template <int RS_, int PS_, bool LONGK_, int MINB_>
+struct Cfg {
+  static constexpr int RS = RS_, PS = PS_, MINB = MINB_;
+  static constexpr bool LONGK = LONGK_;
+};
+// One CTA per SM, 3 raw stages and 2 plane sets (the split of stage t+1 overlaps the MMAs of
+// stage t inside the CTA); the only shape that drains, so every K is allowed.
+using CfgWide = Cfg<RAW_STAGES, PLANE_SETS, true, 1>;
+// Two CTAs per SM for K <= 512: 2 raw stages, 1 plane set and no drain registers (<= 112
+// registers, 97 KB of shared memory); one CTA's epilogue and split overlap the other's MMAs.
+using CfgDual = Cfg<2, 1, false, 2>;
+constexpr int kDualMaxK = 512;
+
+template <class Pb, class C = CfgWide>
 constexpr int smem_bytes() {
-  return RAW_STAGES * (RAW_A + RAW_B) + PLANE_SETS * plane_set_bytes<Pb::A_TMEM>() + 1024 + 128;
+  return C::RS * (RAW_A + RAW_B) + C::PS * plane_set_bytes<Pb::A_TMEM>() + 1024 + 128;
 }
 
 struct Maps {
@@ -131,9 +146,10 @@ constexpr bool kBAll = QRB_TCX_BALL != 0;
 constexpr int TM_A = BN;              // TMEM: accumulator in columns [0, BN), A sets after it
 constexpr int TM_COLS = 256;          // BN + 2 sets x (hi, lo) x BK columns, power of two
 
-template <class Pb>
-__global__ void __launch_bounds__(XTHREADS, 1)
+template <class Pb, class C = CfgWide>
+__global__ void __launch_bounds__(XTHREADS, C::MINB)
     tcx_gemm_kernel(const __grid_constant__ Maps maps, typename Pb::Args a) {
+  constexpr int RAW_STAGES = C::RS, PLANE_SETS = C::PS;
   extern __shared__ __align__(1024) char smraw[];
   char* sm = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   char* rawA = sm;                                  // [RAW_STAGES][RAW_A]
@@ -144,7 +160,7 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(pl0 + PLANE_SETS * PSET);  // [RAW_STAGES]
   uint64_t* mma_bar = full + RAW_STAGES;                                          // [PLANE_SETS]
   uint64_t* pfull = mma_bar + PLANE_SETS;                                         // [PLANE_SETS]
-  static_assert(smem_bytes<Pb>() + BN * 4 <= 227 * 1024, "tcx shared memory");
+  static_assert(smem_bytes<Pb, C>() + BN * 4 <= 227 * 1024 / C::MINB, "tcx shared memory");
   uint32_t* tslot = reinterpret_cast<uint32_t*>(pfull + PLANE_SETS);
 
   const int64_t b = blockIdx.z;
@@ -192,10 +208,10 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   // TMEM accumulation does not round to nearest on each add, and over K = 2048 the drift is
   // large enough to make a Gram indefinite.  Short reductions (nk <= 2 * DRAIN) never drain.
   constexpr int DRAIN = 8;
-  const bool drains = nk > 2 * DRAIN;
-  float racc[BN / 2];
+  const bool drains = C::LONGK && nk > 2 * DRAIN;
+  float racc[C::LONGK ? BN / 2 : 1];
 #pragma unroll
-  for (int i = 0; i < BN / 2; ++i) racc[i] = 0.f;
+  for (int i = 0; i < (C::LONGK ? BN / 2 : 1); ++i) racc[i] = 0.f;
   const int lq = warp & 3;
   bool ok = true;
 
@@ -214,10 +230,10 @@ __global__ void __launch_bounds__(XTHREADS, 1)
       for (int t = 0; t < nk && t < RAW_STAGES; ++t) { issue(t); s_issued = t + 1; }
       constexpr uint32_t IDESC = tc::idesc_tf32(BM, BN);
       for (int t = 0; t < nk; ++t) {
-        const int ps = t & 1;
+        const int ps = t % PLANE_SETS;
         char* pl = pl0 + ps * PSET;
         // on a timeout nothing more is issued; what is in flight is drained below
-        if (!tc::mbar_wait(&pfull[ps], (t >> 1) & 1)) { ok = false; break; }
+        if (!tc::mbar_wait(&pfull[ps], (t / PLANE_SETS) & 1)) { ok = false; break; }
         tc::tc_fence_after();
         QRB_GT(NTHREADS, 4);
         if (t + RAW_STAGES < nk) {  // slot t % RAW_STAGES has been split
@@ -260,12 +276,14 @@ __global__ void __launch_bounds__(XTHREADS, 1)
     QRB_GT(0, 0);
     for (int t = 0; t < nk; ++t) {
       const int s = t % RAW_STAGES, k0 = kb + t * BK;
-      const int ps = t & 1;                 // plane / TMEM set of this stage
+      const int ps = t % PLANE_SETS;        // plane / TMEM set of this stage
       char* pl = pl0 + ps * PSET;
       if (ok && !tc::mbar_wait(&full[s], (t / RAW_STAGES) & 1)) ok = false;
       QRB_GT(0, 1);
-      // set ps was last read by the MMAs of stage t-2 (commit t/2 - 1 on mma_bar[ps])
-      if (t >= 2 && ok && !tc::mbar_wait(&mma_bar[ps], ((t >> 1) - 1) & 1)) ok = false;
+      // set ps was last read by the MMAs of stage t - PLANE_SETS (its commit completed phase
+      // t / PLANE_SETS - 1 of mma_bar[ps])
+      if (t >= PLANE_SETS && ok && !tc::mbar_wait(&mma_bar[ps], ((t / PLANE_SETS) - 1) & 1))
+        ok = false;
       QRB_GT(0, 2);
       if (!Pb::A_TMEM) {
         // all 256 threads: one A and one B micro-block each, both into shared-memory planes
@@ -324,21 +342,23 @@ __global__ void __launch_bounds__(XTHREADS, 1)
                    : "memory");
       QRB_GT(0, 3);
       if (drains && (t + 1) % DRAIN == 0 && t + 1 < nk) {
-        if (ok && !tc::mbar_wait(&mma_bar[ps], (t >> 1) & 1)) ok = false;
+        if (ok && !tc::mbar_wait(&mma_bar[ps], (t / PLANE_SETS) & 1)) ok = false;
         tc::tc_fence_after();
+        if constexpr (C::LONGK) {
 #pragma unroll
-        for (int c = 0; c < BN / 2; c += 32) {
-          float v2[32];
-          tc::tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + (warp >> 2) * (BN / 2) + c, v2);
+          for (int c = 0; c < BN / 2; c += 32) {
+            float v2[32];
+            tc::tmem_ld32(tmem + ((uint32_t)(32 * lq) << 16) + (warp >> 2) * (BN / 2) + c, v2);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) racc[c + i] += v2[i];
+            for (int i = 0; i < 32; ++i) racc[c + i] += v2[i];
+          }
         }
       }
     }
     // the last commit covers every MMA issued before it
     if (nk >= 1 && ok) {
       const int t = nk - 1;
-      if (!tc::mbar_wait(&mma_bar[t & 1], (t >> 1) & 1)) ok = false;
+      if (!tc::mbar_wait(&mma_bar[t % PLANE_SETS], (t / PLANE_SETS) & 1)) ok = false;
     }
     tc::tc_fence_after();
   }
@@ -346,12 +366,14 @@ __global__ void __launch_bounds__(XTHREADS, 1)
   const bool failed = __syncthreads_or(!ok);
   if (failed && issuer_warp && lane == 0) {
     // Drain before the TMEM is freed and the CTA exits: the last commit covers every MMA
-    // issued (commit t completes phase t / 2 of mma_bar[t % 2]), and each of the last
+    // issued (commit t completes phase t / PLANE_SETS of mma_bar[t % PLANE_SETS]), and each
+    // of the last
     // RAW_STAGES TMA stages issued completes phase u / RAW_STAGES of full[u % RAW_STAGES]
     // (parity waits do not consume a phase, so waiting on one already seen is harmless).
     bool drained = true;
     const int nc = s_committed, ni = s_issued;
-    if (nc > 0 && !tc::mbar_wait(&mma_bar[(nc - 1) & 1], ((nc - 1) >> 1) & 1)) drained = false;
+    if (nc > 0 && !tc::mbar_wait(&mma_bar[(nc - 1) % PLANE_SETS], ((nc - 1) / PLANE_SETS) & 1))
+      drained = false;
     for (int u = (ni > RAW_STAGES ? ni - RAW_STAGES : 0); u < ni; ++u)
       if (!tc::mbar_wait(&full[u % RAW_STAGES], (u / RAW_STAGES) & 1)) drained = false;
     if (!drained) s_drained = 0;
@@ -370,8 +392,10 @@ __global__ void __launch_bounds__(XTHREADS, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = 0.f;
       }
+      if constexpr (C::LONGK) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += racc[c + i];
+        for (int i = 0; i < 32; ++i) v[i] += racc[c + i];
+      }
       if (m < M && n0 + col < N) Pb::store(a, b, m, n0 + col, v, M, N);
     }
   }

@@ -21,13 +21,22 @@ static int prep() {
                                    cudaFuncAttributeMaxDynamicSharedMemorySize, kSm);
 }
 
+// dual = 1: the two-CTAs-per-SM shape (K <= 512 only), else the one-CTA shape that drains
 template <class Pb>
 static int tcx_launch(const void* a, bool ak, const void* b, bool bk, int n, int64_t batch,
-                      const typename Pb::Args& args, cudaStream_t s) {
+                      const typename Pb::Args& args, cudaStream_t s, int dual = 0) {
   tcx::Maps mp;
   if (!(ak ? encode_batched(&mp.a, a, n, batch, 128) : encode_batched_wide(&mp.a, a, n, batch)) ||
       !(bk ? encode_batched(&mp.b, b, n, batch, 128) : encode_batched_wide(&mp.b, b, n, batch)))
     return 999;
+  if (dual) {
+    if (n > tcx::kDualMaxK) return 998;
+    cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb, tcx::CfgDual>,
+                         cudaFuncAttributeMaxDynamicSharedMemorySize, tcx::smem_bytes<Pb, tcx::CfgDual>());
+    tcx::tcx_gemm_kernel<Pb, tcx::CfgDual>
+        <<<g128(n, n, batch), tcx::XTHREADS, tcx::smem_bytes<Pb, tcx::CfgDual>(), s>>>(mp, args);
+    return 0;
+  }
   cudaFuncSetAttribute(tcx::tcx_gemm_kernel<Pb>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        tcx::smem_bytes<Pb>());
   tcx::tcx_gemm_kernel<Pb><<<g128(n, n, batch), tcx::XTHREADS, tcx::smem_bytes<Pb>(), s>>>(mp, args);
@@ -38,8 +47,9 @@ extern "C" {
 
 int qrbt_gram(const float* X, float* G, int* info, int64_t batch, int n, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
-  if (use_tc == 2) {
-    if (int e = tcx_launch<tcx::GramX>(X, false, X, false, n, batch, tc::GramTCArgs{n, X, G, info}, s))
+  if (use_tc == 2 || use_tc == 4) {
+    if (int e = tcx_launch<tcx::GramX>(X, false, X, false, n, batch, tc::GramTCArgs{n, X, G, info}, s,
+                                       use_tc == 4))
       return e;
   } else if (use_tc) {
     if (int e = prep<tc::GramTC>()) return e;
@@ -92,9 +102,9 @@ int qrbt_syrk(float* G, const float* R, int* info, int64_t batch, int n, int k0,
 int qrbt_closure(const float* Q, const float* A, const float* sgn, float* H, int* info,
                  int64_t batch, int n, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
-  if (use_tc == 2) {
+  if (use_tc == 2 || use_tc == 4) {
     if (int e = tcx_launch<tcx::ClosureX>(Q, false, A, false, n, batch,
-                                          tc::ClosureTCArgs{n, Q, A, sgn, H, info}, s))
+                                          tc::ClosureTCArgs{n, Q, A, sgn, H, info}, s, use_tc == 4))
       return e;
   } else if (use_tc) {
     if (int e = prep<tc::ClosureTC<float>>()) return e;
@@ -113,8 +123,8 @@ int qrbt_qapply(const float* X, const float* RL, const float* D, float* Q, int* 
                 int64_t batch, int n, int pass2, int use_tc, void* st) {
   cudaStream_t s = (cudaStream_t)st;
   const QApplyArgs qa{n, pass2, X, RL, D, Q, info};
-  if (use_tc == 2) {
-    if (int e = tcx_launch<tcx::QApplyX>(X, true, RL, true, n, batch, qa, s)) return e;
+  if (use_tc == 2 || use_tc == 4) {
+    if (int e = tcx_launch<tcx::QApplyX>(X, true, RL, true, n, batch, qa, s, use_tc == 4)) return e;
   } else if (use_tc) {
     if (int e = prep<tc::QApplyTC>()) return e;
     tc::tc_gemm_kernel<tc::QApplyTC, 128><<<g128(n, n, batch), tc::NTHREADS, kSm, s>>>(qa);

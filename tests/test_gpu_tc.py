@@ -1,6 +1,6 @@
 """GPU unit tests of the GEMM-shaped stages, tcgen05 3xTF32 tiles (register loader = 1,
-TMA-fed = 2, rank-w = 2/3 for the trailing update) and SIMT tiles (0), each against a float64
-product of the same operands.
+TMA-fed = 2, TMA-fed in the two-CTAs-per-SM shape = 4, rank-w = 2/3 for the trailing update) and
+SIMT tiles (0), each against a float64 product of the same operands.
 
 Tolerance: |C - C64| <= 2e-5 * (|A| |B|)_ij + 1e-30 elementwise -- the float32 error bound
 of a K-term dot product (3xTF32 products are accurate to ~2^-21 relative, float32 sums add
@@ -36,7 +36,7 @@ def close(C, C64, bound):
     assert ratio <= 1.0, f"error {ratio:.3g} x bound"
 
 
-@pytest.mark.parametrize("tc", [0, 1, 2])
+@pytest.mark.parametrize("tc", [0, 1, 2, 4])
 @pytest.mark.parametrize("n", [128, 256, 384, 132])
 def test_gram(tc, n):
     g = torch.Generator(device="cuda").manual_seed(n)
@@ -106,7 +106,7 @@ def test_syrk(tc, n, k0, k1):
     close(torch.where(low, G[:, k1:, k1:], 0), torch.where(low, ref, 0), bound)
 
 
-@pytest.mark.parametrize("tc", [0, 1, 2])
+@pytest.mark.parametrize("tc", [0, 1, 2, 4])
 @pytest.mark.parametrize("n", [128, 256, 260])
 def test_closure(tc, n):
     b = 2
@@ -126,7 +126,7 @@ def test_closure(tc, n):
     assert float(torch.tril(H, -1).abs().max()) == 0.0
 
 
-@pytest.mark.parametrize("tc", [0, 1, 2])
+@pytest.mark.parametrize("tc", [0, 1, 2, 4])
 @pytest.mark.parametrize("pass2", [0, 1])
 @pytest.mark.parametrize("n", [128, 384])
 def test_qapply(tc, pass2, n):
