@@ -639,8 +639,11 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   tcx::Maps cm;
   const bool cx = tcp && std::is_same<T, float>::value && tcx_maps(cm, ws.L, false, A, false, n, cb);
   QRB_LAUNCH(prof, F_CLOSURE,
+             // the closure keeps the one-CTA shape at every K: its epilogue waits on global
+             // loads of A, and two CTAs per SM measured slower (2.51 -> 2.59 ms, n = 512)
              if (cx) launch_tcx<tcx::ClosureX>(tc_grid(n, n, cb), cm,
-                                               tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info}, n, st);
+                                               tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info},
+                                               tcx::kDualMaxK + 1, st);
              else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>
                  <<<tc_grid(n, n, cb), tc::NTHREADS, kTcSmem, st>>>(
                      tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
