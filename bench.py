@@ -65,6 +65,11 @@ def parse():
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--quick", action="store_true",
                    help="headline only: no extra configurations, GPU context or gates")
+    p.add_argument("--ref-kernels", action="store_true",
+                   help="context only: time the reference's own CUDA stage kernels "
+                        "(kan_metric/kqr_fused.py fused_qr, kan_metric/kqr_cluster_kan.py "
+                        "cluster_qr; JIT-compiled from baseline/_ref) against qrb200 on the same "
+                        "inputs, print one JSON line and exit")
     p.add_argument("--profile-run", action="store_true",
                    help="one warm-up call and one measured call of the library, nothing else "
                         "(the command the ncu summaries under profiles/ are taken on)")
@@ -717,8 +722,59 @@ def run_qrb(args):
         dist.destroy_process_group()
 
 
+def run_ref_kernels(args):
+    """Same-box comparison with the reference's hand-written CUDA kernels for this pipeline:
+    its fully fused one-block-per-matrix kernel (kan_metric/kqr_fused.py:230-305, FP32 Gram
+    build GRAM_MODE=0) on the small-n batches of config 2, and its 16-CTA cluster kernel
+    (kan_metric/kqr_cluster_kan.py:308-365, cluster_qr with C = 16) on n = 512.  Both are
+    JIT-compiled by the reference's own load_inline calls from the unmodified copies under
+    baseline/_ref.  Timed with CUDA events after a warm-up call; gated on the device."""
+    import qrb200
+    from qrb200 import checker
+    from qrb200 import generators as G
+    dev = torch.device("cuda", 0)
+    sys.dont_write_bytecode = True
+    sys.path[:0] = [str(REF_DIR / "kan_metric"), str(REF_DIR)]
+    out = {"ref_kernels": {}}
+    import kqr_fused  # the reference module (compiles kqr.py's modlu kernel on import)
+    fused = kqr_fused._build(0)
+    for n, seed in ((32, 1), (64, 1), (128, 2)):
+        A = G.gaussian((16384, n, n), seed=seed, device=dev)
+        r = {}
+        ms_ref = dev_time(lambda: fused.fused_qr(A, 1), dev, reps=3, warm=1)
+        H, tau = fused.fused_qr(A, 1)
+        r["reference_fused_qr"] = {"ms": ms_ref, "matrices_per_s": A.shape[0] / (ms_ref / 1e3),
+                                   "gates_first_512": checker.summary(A[:512], H[:512], tau[:512])}
+        ms_q = dev_time(lambda: qrb200.geqrf(A), dev, reps=3, warm=1)
+        Hq, tq, _ = qrb200.geqrf(A)
+        r["qrb200"] = {"ms": ms_q, "matrices_per_s": A.shape[0] / (ms_q / 1e3),
+                       "gates_first_512": checker.summary(A[:512], Hq[:512], tq[:512])}
+        out["ref_kernels"][f"fused_n{n}_b16384"] = r
+        del A, H, tau, Hq, tq
+    import kqr_cluster_kan
+    cl = kqr_cluster_kan._build(4, 3)
+    A = G.heterogeneous(1536, 512, seed=3, device=dev)
+    r = {}
+    ms_ref = dev_time(lambda: cl.cluster_qr(A, 16), dev, reps=1, warm=1)
+    H, tau = cl.cluster_qr(A, 16)
+    r["reference_cluster_qr_C16"] = {"ms": ms_ref, "matrices_per_s": A.shape[0] / (ms_ref / 1e3),
+                                     "gates": checker.summary(A, H, tau)}
+    ms_q = dev_time(lambda: qrb200.geqrf(A), dev, reps=3, warm=1)
+    Hq, tq, _ = qrb200.geqrf(A)
+    r["qrb200"] = {"ms": ms_q, "matrices_per_s": A.shape[0] / (ms_q / 1e3),
+                   "gates": checker.summary(A, Hq, tq)}
+    out["ref_kernels"]["hetero_n512_b1536"] = r
+    out["note"] = ("context, not a benchmark arm: the reference's CUDA stage kernels against "
+                   "qrb200 on the same inputs on one B200; the cluster kernel's timing includes "
+                   "the cudaDeviceSynchronize inside its host wrapper")
+    print(json.dumps(out), flush=True)
+
+
 def main():
     args = parse()
+    if args.ref_kernels:
+        run_ref_kernels(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -320,6 +320,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
         }
       }
     }
+    QRB_PT(5);
     if (tid < w) a.D[b * n + k0 + tid] = dpiv[tid];
     // rows [k0, k0+w) of L_G^{-1} before this panel (identity block included), columns < k1;
     // one flat float4 copy over all threads (k0 % 4 == 0 here since n % 4 == 0 or k0 == 0)
@@ -350,6 +351,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
         }
       }
     }
+    QRB_PT(6);
     // L11^{-1} (unit lower) into rows [k0, k0+w) of the W buffer: row i of L11^{-1} is
     // e_i^T L11^{-1}, computed by thread i in the registers of its (pivot) row, which is done
     if (tid < w) {
