@@ -184,6 +184,25 @@ def geqrf_host(data: torch.Tensor, out=None, sub_batch: int = 0):
     return H, tau, info
 
 
+_OPS_LOADED = False
+
+
+def load_torch_ops():
+    """Register ``torch.ops.qrb200.geqrf(A) -> (H, tau, info)`` (the TORCH_LIBRARY operator in
+    ``libqrb200_torch_ops.so``, a thin layer over the C ABI with CUDA and Meta kernels) and
+    return the operator.  Raises if the library was not built."""
+    global _OPS_LOADED
+    from pathlib import Path
+    if not _OPS_LOADED:
+        path = Path(__file__).resolve().parent / "libqrb200_torch_ops.so"
+        if not path.exists():
+            raise ImportError(f"{path} is not built; run `python -m qrb200.build`")
+        _lib.lib()  # the C ABI library the operator links to
+        torch.ops.load_library(str(path))
+        _OPS_LOADED = True
+    return torch.ops.qrb200.geqrf
+
+
 def raise_on_info(info: torch.Tensor) -> None:
     """Raise ``LinAlgError`` like torch.linalg.cholesky would (one device->host read)."""
     bad = (info & (_lib.INFO_CHOL1_NOT_PD | _lib.INFO_CHOL2_NOT_PD)) != 0

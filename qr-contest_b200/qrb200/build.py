@@ -33,7 +33,8 @@ def nvcc() -> str:
 
 
 def sources():
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
+    return (sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.cpp"))
+            + sorted(INCLUDE.glob("*.h")))
 
 
 def up_to_date(target: Path) -> bool:
@@ -50,11 +51,37 @@ def _compile(src: Path, out: Path, verbose: bool, extra) -> None:
     subprocess.run(cmd, check=True)
 
 
+OPS = PKG / "libqrb200_torch_ops.so"  # torch.ops.qrb200.geqrf (links libqrb200.so)
+
+
+def _compile_ops(verbose: bool) -> None:
+    """The TORCH_LIBRARY operator library: g++ against torch's headers and libraries, linked
+    to libqrb200.so next to it (rpath $ORIGIN).  No CUDA code is compiled here."""
+    import torch
+    from torch.utils import cpp_extension as ce
+    cuda_home = Path(ce.CUDA_HOME or "/usr/local/cuda")
+    abi = int(torch.compiled_with_cxx11_abi())
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-I", str(INCLUDE), "-I", str(cuda_home / "include")]
+    for d in ce.include_paths():
+        cmd += ["-I", d]
+    cmd += ["-o", str(OPS), str(CSRC / "qrb_torch_op.cpp"), "-L", str(PKG), "-l:libqrb200.so",
+            "-Wl,-rpath,$ORIGIN"]
+    for d in ce.library_paths():
+        cmd += ["-L", d, f"-Wl,-rpath,{d}"]
+    cmd += ["-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch"]
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+
+
 def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
     for src, out, defs in ((CSRC / "qrb_api.cu", LIB, []),
                            (CSRC / "qrb_testkit.cu", TESTKIT, ["-DQRB_PANEL_TIMERS"])):
         if force or not up_to_date(out):
             _compile(src, out, verbose, [*extra, *defs])
+    if force or not up_to_date(OPS) or OPS.stat().st_mtime < (CSRC / "qrb_torch_op.cpp").stat().st_mtime:
+        _compile_ops(verbose)
     return LIB
 
 

@@ -148,3 +148,14 @@ def test_noalloc_order_limit_without_gpu():
     assert call(n4) == _lib.QRB200_ERR_INVALID_ARG
     assert call(n4 + 4) == _lib.QRB200_ERR_SCRATCH_LIMIT
     assert call(64) == _lib.QRB200_ERR_INVALID_ARG
+
+
+def test_torch_operator_registers_and_has_meta_shapes():
+    # torch.ops.qrb200.geqrf loads without a GPU; its Meta kernel gives the output shapes
+    import torch
+    from qrb200 import api
+    op = api.load_torch_ops()
+    A = torch.empty(2, 3, 40, 40, device="meta", dtype=torch.bfloat16)
+    H, tau, info = op(A)
+    assert H.shape == (2, 3, 40, 40) and tau.shape == (2, 3, 40) and info.shape == (2, 3)
+    assert H.dtype == torch.bfloat16 and tau.dtype == torch.bfloat16 and info.dtype == torch.int32

@@ -474,3 +474,17 @@ def test_rect_classes_bf16_and_errors():
         qrb().geqrf_rect(A.mT.contiguous())
     rc = _lib.lib().qrb200_geqrf_batched_rect(1, 1, 1, 1, 1, 8, 9, _lib.QRB200_F32, None)
     assert rc == _lib.QRB200_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
+def test_torch_operator_matches_entry_point(dtype):
+    """torch.ops.qrb200.geqrf (TORCH_LIBRARY operator over the C ABI) returns exactly what
+    qrb200.geqrf returns, on the current stream, with leading dims."""
+    op = qrb().api.load_torch_ops()
+    g = torch.Generator(device="cuda").manual_seed(81)
+    A = torch.randn(3, 2, 96, 96, device="cuda", generator=g).to(dtype)
+    H, tau, info = op(A)
+    H0, t0, i0 = qrb().geqrf(A)
+    torch.cuda.synchronize()
+    assert H.dtype == dtype and H.shape == A.shape and tau.shape == (3, 2, 96)
+    assert torch.equal(H, H0) and torch.equal(tau, t0) and torch.equal(info, i0)
