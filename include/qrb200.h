@@ -40,6 +40,9 @@ extern "C" {
 #define QRB200_INFO_CHOL2_NOT_PD 4    /* 2nd pass */
 #define QRB200_INFO_LU_ZERO_PIVOT 8   /* exactly singular column met (informational) */
 #define QRB200_INFO_DEVICE_TIMEOUT 16 /* a bounded in-kernel wait expired (never expected) */
+#define QRB200_INFO_BOUNDS 32         /* bounds-check build (libqrb200_checked.so) only: a row
+                                         index read from the LU's pivot maps was out of range;
+                                         the access was redirected inside the buffer */
 
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int qrb200_version(void);

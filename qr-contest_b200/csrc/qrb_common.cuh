@@ -27,7 +27,23 @@ enum InfoBits : int {
   INFO_CHOL2_NOT_PD = 4,      // second pass
   INFO_LU_ZERO_PIVOT = 8,     // an exactly singular column (informational, like getrf info>0)
   INFO_DEVICE_TIMEOUT = 16,   // a bounded in-kernel wait gave up (never expected)
+  INFO_BOUNDS = 32,           // bounds-check build: a pivot-map row index was out of range
 };
+
+// Row indices read from the LU's pivot maps (srcmap, orig, the panels' position maps) are the
+// only data-dependent indices of the pipeline.  The bounds-check build (-DQRB_BOUNDS_CHECK,
+// libqrb200_checked.so) tests each against its range; an index outside it raises INFO_BOUNDS
+// in the matrix's info word and is replaced by `lo`, so the access stays inside the buffer and
+// nothing traps.  In the regular build this is the identity.
+__device__ __forceinline__ int checked_row(int r, int lo, int hi, int* info) {
+#ifdef QRB_BOUNDS_CHECK
+  if (r < lo || r >= hi) {
+    if (info) atomicOr(info, INFO_BOUNDS);
+    return lo;
+  }
+#endif
+  return r;
+}
 
 __device__ __forceinline__ float to_f32(float x) { return x; }
 __device__ __forceinline__ float to_f32(__nv_bfloat16 x) { return __bfloat162float(x); }

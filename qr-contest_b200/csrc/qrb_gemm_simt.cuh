@@ -37,7 +37,7 @@ struct TrailW {
   }
   __device__ static bool live(int, int) { return true; }
   __device__ static int srow(const Args& a, int64_t b, int r) {
-    return a.srcmap ? a.srcmap[b * a.n + r] : r;
+    return a.srcmap ? checked_row(a.srcmap[b * a.n + r], 0, a.n, nullptr) : r;
   }
   // A(m, k) = W[k1+m][k]
   __device__ static float ldA(const Args& a, int64_t b, int k, int m) {

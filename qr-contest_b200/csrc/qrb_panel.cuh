@@ -209,10 +209,10 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
   // ---- outputs ----
   if (MODE == PM_PIVOT) {
     int* orig = a.orig + b * n;
-    for (int r = tid; r < m; r += 256) oid[r] = (k0 == 0) ? r : orig[k0 + r];
+    for (int r = tid; r < m; r += 256) oid[r] = (k0 == 0) ? r : checked_row(orig[k0 + r], 0, n, info);
     __syncthreads();
     for (int r = tid; r < m; r += 256) {
-      const int o = oid[lid[r]];
+      const int o = oid[checked_row(lid[r], 0, m, info)];
       nid[r] = o;
       orig[k0 + r] = o;
       a.srcmap[b * n + k0 + r] = k0 + lid[r];

@@ -251,11 +251,11 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(256, 2)
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
       const int r = rbase + tid + 256 * q;
-      if (r < m) oids[tid + 256 * q] = (k0 == 0) ? r : orig[k0 + r];
+      if (r < m) oids[tid + 256 * q] = (k0 == 0) ? r : checked_row(orig[k0 + r], 0, n, a.info + b);
     }
     cluster.sync();  // every CTA read its original ids before any is overwritten
     for (int p = rbase + tid; p < m && p < rbase + kClRows; p += 256) {
-      const int r = posrow[p];
+      const int r = checked_row(posrow[p], 0, m, a.info + b);
       orig[k0 + p] = *cluster.map_shared_rank(&oids[r % kClRows], r / kClRows);
       a.srcmap[b * n + k0 + p] = k0 + r;
     }

@@ -265,11 +265,11 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
       const int r = tid + 256 * q;
-      if (r < m) oids[r] = (k0 == 0) ? r : orig[k0 + r];
+      if (r < m) oids[r] = (k0 == 0) ? r : checked_row(orig[k0 + r], 0, n, a.info + b);
     }
     __syncthreads();
     for (int p = tid; p < m; p += 256) {
-      const int r = posrow[p];
+      const int r = checked_row(posrow[p], 0, m, a.info + b);
       orig[k0 + p] = oids[r];
       a.srcmap[b * n + k0 + p] = k0 + r;
     }

@@ -129,7 +129,7 @@ struct RWTrail {
   }
   __device__ static bool live(const Args&, int, int) { return true; }
   __device__ static int srow(const Args& a, int64_t b, int r) {
-    return a.srcmap ? a.srcmap[b * a.n + r] : r;
+    return a.srcmap ? checked_row(a.srcmap[b * a.n + r], 0, a.n, a.info + b) : r;
   }
   __device__ static const float* a_ptr(const Args& a, int64_t b, int m) {
     return a.W + ((int64_t)b * a.n + a.k1 + m) * a.ldw;

@@ -162,7 +162,7 @@ struct TrailWTC {
     ke = a.k1 - a.k0;
   }
   __device__ static int srow(const Args& a, int64_t b, int r) {
-    return a.srcmap ? a.srcmap[b * a.n + r] : r;
+    return a.srcmap ? checked_row(a.srcmap[b * a.n + r], 0, a.n, a.info + b) : r;
   }
   __device__ static void loadA(const Args& a, int64_t b, int m0, int k0, float (&v)[4][4]) {
     const int M = a.n - a.k1, K = a.k1 - a.k0;

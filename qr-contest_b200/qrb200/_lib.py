@@ -10,6 +10,8 @@ import ctypes
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libqrb200.so"
+# the same library built with -DQRB_BOUNDS_CHECK (pivot-map indices checked, INFO_BOUNDS)
+CHECKED_LIB_PATH = Path(__file__).resolve().parent / "libqrb200_checked.so"
 
 QRB200_OK = 0
 QRB200_ERR_INVALID_ARG = 1
@@ -30,6 +32,7 @@ INFO_CHOL1_NOT_PD = 2
 INFO_CHOL2_NOT_PD = 4
 INFO_LU_ZERO_PIVOT = 8
 INFO_DEVICE_TIMEOUT = 16
+INFO_BOUNDS = 32
 
 OPT_GEMM_PATH = 1
 OPT_SMALL_N = 2

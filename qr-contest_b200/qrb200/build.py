@@ -19,6 +19,7 @@ CSRC = ROOT / "csrc"
 INCLUDE = ROOT.parent / "include"
 LIB = PKG / "libqrb200.so"
 TESTKIT = PKG / "libqrb200_testkit.so"   # single-stage entry points for the GPU unit tests
+CHECKED = PKG / "libqrb200_checked.so"   # the library with the pivot-map bounds checks
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-shared",
@@ -77,6 +78,7 @@ def _compile_ops(verbose: bool) -> None:
 
 def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
     for src, out, defs in ((CSRC / "qrb_api.cu", LIB, []),
+                           (CSRC / "qrb_api.cu", CHECKED, ["-DQRB_BOUNDS_CHECK"]),
                            (CSRC / "qrb_testkit.cu", TESTKIT, ["-DQRB_PANEL_TIMERS"])):
         if force or not up_to_date(out):
             _compile(src, out, verbose, [*extra, *defs])
