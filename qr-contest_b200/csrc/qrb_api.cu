@@ -371,7 +371,8 @@ static cudaError_t ensure_attrs() {
 template <int MODE, typename TIn, typename TOut>
 static void launch_panel(const PanelArgs& pa, int64_t cb, cudaStream_t st) {
   const int m = pa.n - pa.k0;
-  if (m <= 256) panel_reg_kernel<MODE, TIn, TOut, 1><<<(unsigned)cb, 256, 0, st>>>(pa);
+  if (m <= 128) panel_reg_kernel<MODE, TIn, TOut, 1, 128><<<(unsigned)cb, 128, 0, st>>>(pa);
+  else if (m <= 256) panel_reg_kernel<MODE, TIn, TOut, 1><<<(unsigned)cb, 256, 0, st>>>(pa);
   else if (m <= 512) panel_reg_kernel<MODE, TIn, TOut, 2><<<(unsigned)cb, 256, 0, st>>>(pa);
   else if (cluster_panel(pa.n) && m <= 2 * kClRows)
     panel_cl_kernel<MODE, TIn, TOut, 2><<<(unsigned)(2 * cb), 256, 0, st>>>(pa);

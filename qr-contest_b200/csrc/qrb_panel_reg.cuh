@@ -67,8 +67,12 @@ __device__ __forceinline__ void times_l11_inv(float (&x)[PR_W], const float (*Ls
   }
 }
 
-template <int MODE, typename TIn, typename TOut, int RPT>
-__global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(PanelArgs a) {
+// NT threads per CTA (256; 128 for panels of at most 128 rows, which then fit twice as many
+// CTAs per SM).
+template <int MODE, typename TIn, typename TOut, int RPT, int NT = 256>
+__global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
+    panel_reg_kernel(PanelArgs a) {
+  constexpr int NWARP = NT / 32;
   const int n = a.n, k0 = a.k0, w = a.w, m = n - k0;
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -76,11 +80,11 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   __shared__ float prow[2][PR_W];
   __shared__ float Ls[PR_W][PR_W + 1];   // multipliers of the pivot rows, by position
   __shared__ float dpiv[PR_W];
-  __shared__ float red_v[2][8];
-  __shared__ int red_p[2][8], red_r[2][8];
-  __shared__ int rowpos[256 * RPT], posrow[256 * RPT];  // PIVOT: local row <-> position
-  __shared__ int oids[256 * RPT];
-  __shared__ float tpart[8][PR_W];
+  __shared__ float red_v[2][NWARP];
+  __shared__ int red_p[2][NWARP], red_r[2][NWARP];
+  __shared__ int rowpos[NT * RPT], posrow[NT * RPT];  // PIVOT: local row <-> position
+  __shared__ int oids[NT * RPT];
+  __shared__ float tpart[NWARP][PR_W];
   __shared__ int s_flags;
   __shared__ float s_mu;
 
@@ -92,13 +96,13 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   if (MODE == PM_CHOL) {
     if (k0 == 0) {
       float acc = 0.f;
-      for (int i = tid; i < (a.nmu > 0 ? a.nmu : n); i += 256) acc += to_f32(src[(int64_t)i * n + i]);
+      for (int i = tid; i < (a.nmu > 0 ? a.nmu : n); i += NT) acc += to_f32(src[(int64_t)i * n + i]);
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_down_sync(0xffffffffu, acc, o);
       if (lane == 0) red_v[0][warp] = acc;
       __syncthreads();
       if (tid == 0) {
         float t = 0.f;
-        for (int i = 0; i < 8; ++i) t += red_v[0][i];
+        for (int i = 0; i < NWARP; ++i) t += red_v[0][i];
         s_mu = 1e-7f * (t / (float)(a.nmu > 0 ? a.nmu : n));
         a.mu[b] = s_mu;
       }
@@ -113,14 +117,14 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   bool live[RPT];
 #pragma unroll
   for (int q = 0; q < RPT; ++q) {
-    const int r = tid + 256 * q;
+    const int r = tid + NT * q;
     live[q] = r < m;
     if (r < m) load_row32(src + (int64_t)(k0 + r) * n + k0, w, vec, x[q]);
     else {
 #pragma unroll
       for (int c = 0; c < PR_W; ++c) x[q][c] = 0.f;
     }
-    if (MODE == PM_PIVOT && r < 256 * RPT) { rowpos[r] = r; posrow[r] = r; }
+    if (MODE == PM_PIVOT && r < NT * RPT) { rowpos[r] = r; posrow[r] = r; }
   }
   __syncthreads();
 
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
 #pragma unroll
       for (int q = 0; q < RPT; ++q) {
         if (live[q]) {
-          const int r = tid + 256 * q;
+          const int r = tid + NT * q;
           const float xv = x[q][c];
           bad |= !isfinite(xv);
           const unsigned v = isnan(xv) ? 0u : __float_as_uint(fabsf(xv));
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
       unsigned V = __float_as_uint(red_v[par][0]);
       int Pp = red_p[par][0], Rw = red_r[par][0];
 #pragma unroll
-      for (int i = 1; i < 8; ++i) {
+      for (int i = 1; i < NWARP; ++i) {
         const unsigned vi = __float_as_uint(red_v[par][i]);
         const int pi = red_p[par][i];
         if (vi > V || (vi == V && pi < Pp)) { V = vi; Pp = pi; Rw = red_r[par][i]; }
@@ -169,7 +173,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
       // the winner publishes its row (U row c and its multipliers for columns < c)
 #pragma unroll
       for (int q = 0; q < RPT; ++q) {
-        if (tid + 256 * q == Rw) {
+        if (tid + NT * q == Rw) {
 #pragma unroll
           for (int j = 0; j < PR_W; ++j) {
             if (j < w) prow[par][j] = x[q][j];
@@ -236,7 +240,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
       }
 #pragma unroll
       for (int q = 0; q < RPT; ++q) {
-        const int r = tid + 256 * q;
+        const int r = tid + NT * q;
         if (r > c && r < m) {
           // Cholesky scales by the reciprocal pivot (as potf2 does); the chart divides (:158)
           const float l = (MODE == PM_CHOL) ? x[q][c] * rpiv : (-sgn * x[q][c]) / piv;
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   int pos[RPT];
 #pragma unroll
   for (int q = 0; q < RPT; ++q) {
-    const int r = tid + 256 * q;
+    const int r = tid + NT * q;
     pos[q] = (MODE == PM_PIVOT && r < m) ? rowpos[r] : r;
   }
   float* Wb = a.W + (int64_t)b * n * a.ldw;
@@ -264,11 +268,11 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
     int* orig = a.orig + b * n;
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
-      const int r = tid + 256 * q;
+      const int r = tid + NT * q;
       if (r < m) oids[r] = (k0 == 0) ? r : checked_row(orig[k0 + r], 0, n, a.info + b);
     }
     __syncthreads();
-    for (int p = tid; p < m; p += 256) {
+    for (int p = tid; p < m; p += NT) {
       const int r = checked_row(posrow[p], 0, m, a.info + b);
       orig[k0 + p] = oids[r];
       a.srcmap[b * n + k0 + p] = k0 + r;
@@ -276,7 +280,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
     float* L = a.L + mat_off(b, n);
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
-      const int r = tid + 256 * q;
+      const int r = tid + NT * q;
       if (r >= m) continue;
       float* Lrow = L + (int64_t)oids[r] * n;
       const int p = pos[q];
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
-      const int r = tid + 256 * q;
+      const int r = tid + NT * q;
       if (r >= m) continue;
 #pragma unroll
       for (int c = 0; c < PR_W; ++c)
@@ -329,7 +333,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
       if (vec && (cols & 3) == 0) {
         const int per = cols >> 2;
 #pragma unroll 4
-        for (int idx = tid; idx < w * per; idx += 256) {
+        for (int idx = tid; idx < w * per; idx += NT) {
           const int c = idx / per, j = (idx - c * per) * 4;
           float4 v;
           if (j + 3 < k0) {
@@ -344,7 +348,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
           *reinterpret_cast<float4*>(a.Bp + ((int64_t)b * a.ldw + c) * n + j) = v;
         }
       } else {
-        for (int idx = tid; idx < w * cols; idx += 256) {
+        for (int idx = tid; idx < w * cols; idx += NT) {
           const int c = idx / cols, j = idx - c * cols;
           a.Bp[((int64_t)b * a.ldw + c) * n + j] =
               (j < k0) ? R[(int64_t)(k0 + c) * n + j] : ((j == k0 + c) ? 1.f : 0.f);
@@ -367,7 +371,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
     for (int c = 0; c < PR_W; ++c) part[c] = 0.f;
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
-      const int r = tid + 256 * q;
+      const int r = tid + NT * q;
       if (r >= m) continue;
       TOut* Hrow = H + (int64_t)(k0 + r) * n + k0;
       if (r >= PR_W && w == PR_W && vec) {  // whole row below the panel: vector stores
@@ -405,7 +409,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
     if (tid < w) {
       float acc = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc += tpart[i][tid];
+      for (int i = 0; i < NWARP; ++i) acc += tpart[i][tid];
       reinterpret_cast<TOut*>(a.tau)[b * n + k0 + tid] = from_f32<TOut>(2.f / (acc + 1.f));
       a.s[b * n + k0 + tid] = dpiv[tid];
     }
@@ -416,7 +420,7 @@ __global__ void __launch_bounds__(256, (RPT == 1 ? 3 : 2)) panel_reg_kernel(Pane
   if (k0 + w < n) {
 #pragma unroll
     for (int q = 0; q < RPT; ++q) {
-      const int r = tid + 256 * q;
+      const int r = tid + NT * q;
       if (r < m && pos[q] >= w) {
         times_l11_inv(x[q], Ls, w);
         store_row32(Wb + (int64_t)(k0 + pos[q]) * a.ldw, w, (a.ldw & 3) == 0, x[q]);
