@@ -463,7 +463,15 @@ def measure_c4(dev):
     rate = b / (ms / 1e3)
     tf = rate * algo_flops(n) / 1e12
     gates = checker.summary(A[:4], H[:4], tau[:4], chunk=2)
+    from qrb200 import _lib
+    Hh, th = torch.empty_like(A), torch.empty(b, n, device=dev)
+    inf = torch.zeros(b, dtype=torch.int32, device=dev)
+    _, fam = _lib.geqrf_batched_timed(A.data_ptr(), Hh.data_ptr(), th.data_ptr(), inf.data_ptr(),
+                                      b, n, _lib.QRB200_F32, ws.data_ptr(), ws.numel(),
+                                      torch.cuda.current_stream(dev).cuda_stream)
+    del Hh, th, inf
     r = {"matrices": b, "n": n, "ms": ms, "matrices_per_s": rate, "tflops_7n3": tf,
+         "family_ms": {k: round(v, 3) for k, v in fam.items() if v > 0},
          "tensor_frac": tf / (bf16 / 6), "info_nonzero": int((info != 0).sum()),
          "gates_first_4": gates}
     del A, ws, H, tau, info, out
@@ -691,14 +699,17 @@ def run_qrb(args):
     if not args.quick:
         del ws
         torch.cuda.empty_cache()
-        extra["c5"] = measure_c5(dev, rank, world)
-        torch.cuda.empty_cache()
         if world == 1:
+            # the single-GPU configs run before the sweep: after the sweep's ~40 GB of
+            # allocations the n = 2048 batch measured 40 % slower in the same process
             extra["c2"] = measure_c2(dev)
             torch.cuda.empty_cache()
             extra["c4"] = measure_c4(dev)
             torch.cuda.empty_cache()
             extra["gpu_context"] = gpu_context(A, dev)
+            torch.cuda.empty_cache()
+        extra["c5"] = measure_c5(dev, rank, world)
+        torch.cuda.empty_cache()
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
