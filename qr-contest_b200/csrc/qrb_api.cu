@@ -427,6 +427,7 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
       pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = ldw;
       pa.src = ws.T0; pa.R = ws.R; pa.D = ws.D; pa.W = Wp; pa.Wc = Wcp; pa.Bp = Bpp;
       pa.mu = ws.mu; pa.nmu = nmu; pa.info = info; pa.info_bit = info_bit;
+      pa.bp_ready = blk && k0 > kb;  // stored by the previous panel's L_G^{-1} update
       QRB_LAUNCH(prof, F_CHOL_PANEL,
                  (launch_panel<PM_CHOL, float, float>(pa, cb, st)));
       const int k1 = k0 + w;
@@ -439,10 +440,14 @@ static void cholqr_pass(const float* X, float* Q, int n, int64_t cb, int nb, con
                        RWSyrkArgs{n, k0, k1, ldw, ws.T0, ws.R, Wcp, info, n});
                    else simt_gemm_kernel<TrailSyrk><<<tiles_grid(n - k1, n - k1, cb), 256, 0, st>>>(
                        TrailSyrkArgs{n, k0, k1, ws.T0, ws.R}));
+      RWLinvArgs lv{n, k0, k1, ldw, ws.R, Wp, Bpp, info, ke};
+      if (blk && k1 < ke) {  // the next panel of this block takes its snapshot from here
+        lv.Bn = Bpp + (size_t)w * n;
+        lv.wn = (n - k1 < nb) ? n - k1 : nb;
+      }
       QRB_LAUNCH(prof, F_CHOL_TRAIL,
                  if (tcp && rw) tc::tc_rankw_kernel<RWLinv>
-                     <<<rwt_grid(ke - k0, k1, cb), 256, tc::RWT_SMEM, st>>>(
-                         RWLinvArgs{n, k0, k1, ldw, ws.R, Wp, Bpp, info, ke});
+                     <<<rwt_grid(ke - k0, k1, cb), 256, tc::RWT_SMEM, st>>>(lv);
                  else if (rw) rankw_kernel<RWLinv><<<rw_grid(n - k0, k1, cb), 256, 0, st>>>(
                      RWLinvArgs{n, k0, k1, ldw, ws.R, Wp, Bpp, info, n});
                  else simt_gemm_kernel<LinvTrail><<<tiles_grid(n - k0, k1, cb), 256, 0, st>>>(

@@ -54,6 +54,7 @@ struct PanelArgs {
   float* Wc;         // CHOL: [b][n][ldw] out, rows [k0+w, n): L21 D^{1/2}
   float* Bp;         // CHOL: [b][ldw][n] out, rows of L_G^{-1} [k0, k0+w) before the panel
                      //       (columns < k0+w, identity block included)
+  int bp_ready;      // CHOL: Bp's columns < k0 were already written by the previous update
   float* mu;         // CHOL: [b] jitter, computed when k0 == 0
   int nmu;           // CHOL: diagonal entries in the jitter's mean (0 = n; the rectangular
                      //       entry point's zero-padded columns are left out of it)
@@ -240,7 +241,7 @@ __global__ void __launch_bounds__(256) panel_kernel(PanelArgs a) {
     for (int c = warp; c < w; c += 8) {
       float* bp = a.Bp + ((int64_t)b * a.ldw + c) * n;
       const float* rl = R + (int64_t)(k0 + c) * n;
-      for (int j = lane; j < k0 + w; j += 32)
+      for (int j = (a.bp_ready ? k0 : 0) + lane; j < k0 + w; j += 32)
         bp[j] = (j < k0) ? rl[j] : ((j == k0 + c) ? 1.f : 0.f);
     }
     // L11^{-1} (unit lower) into rows [k0, k0+w) of the W buffer

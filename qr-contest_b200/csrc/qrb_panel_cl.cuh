@@ -308,9 +308,10 @@ __global__ void __cluster_dims__(CL, 1, 1) __launch_bounds__(256, 2)
     if (rank == 0) {
       if (tid < w) a.D[b * n + k0 + tid] = dpiv[tid];
       // rows [k0, k0+w) of L_G^{-1} before this panel (identity block included), cols < k1
-      const int cols = k0 + w;
+      const int j0 = a.bp_ready ? k0 : 0;  // columns < k0 already stored by the update
+      const int cols = k0 + w - j0;
       for (int idx = tid; idx < w * cols; idx += 256) {
-        const int c = idx / cols, j = idx - c * cols;
+        const int c = idx / cols, j = j0 + idx - c * cols;
         a.Bp[((int64_t)b * a.ldw + c) * n + j] =
             (j < k0) ? R[(int64_t)(k0 + c) * n + j] : ((j == k0 + c) ? 1.f : 0.f);
       }

@@ -329,12 +329,14 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
     // rows [k0, k0+w) of L_G^{-1} before this panel (identity block included), columns < k1;
     // one flat float4 copy over all threads (k0 % 4 == 0 here since n % 4 == 0 or k0 == 0)
     {
-      const int cols = k0 + w;
+      // columns [j0, k0 + w): with bp_ready the previous update already stored columns < k0
+      const int j0 = a.bp_ready ? k0 : 0;
+      const int cols = k0 + w - j0;
       if (vec && (cols & 3) == 0) {
         const int per = cols >> 2;
 #pragma unroll 4
         for (int idx = tid; idx < w * per; idx += NT) {
-          const int c = idx / per, j = (idx - c * per) * 4;
+          const int c = idx / per, j = j0 + (idx - c * per) * 4;
           float4 v;
           if (j + 3 < k0) {
             v = *reinterpret_cast<const float4*>(R + (int64_t)(k0 + c) * n + j);
@@ -349,7 +351,7 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
         }
       } else {
         for (int idx = tid; idx < w * cols; idx += NT) {
-          const int c = idx / cols, j = idx - c * cols;
+          const int c = idx / cols, j = j0 + idx - c * cols;
           a.Bp[((int64_t)b * a.ldw + c) * n + j] =
               (j < k0) ? R[(int64_t)(k0 + c) * n + j] : ((j == k0 + c) ? 1.f : 0.f);
         }

@@ -197,6 +197,11 @@ struct RWLinvArgs {
   const float* Bp;  // [ldw][n] per matrix: raw panel rows, columns [0, k1)
   int* info;
   int lim;          // rows [k0, lim) are updated (n: every row below the panel)
+  // Next panel's snapshot slot ([ldw][n] per matrix, like Bp) or nullptr: rows [k1, k1 + wn)
+  // of the result, columns < k1, are the next panel's rows of L_G^{-1} "before the panel"; they
+  // are stored there as well, so the next panel does not copy them back out of RL.
+  float* Bn = nullptr;
+  int wn = 0;
 };
 struct RWLinv {
   using Args = RWLinvArgs;
@@ -230,6 +235,7 @@ struct RWLinv {
         if (j + q < r) p[q] = t[q];
     } else {
       st4(p, x);
+      if (a.Bn && r < a.k1 + a.wn) st4(a.Bn + ((int64_t)b * a.ldw + (r - a.k1)) * a.n + j, x);
     }
   }
 };
