@@ -145,11 +145,6 @@ long long qrb200_launch_count(void);
  *   the rest of the trailing matrix takes one float32 K = block update per block.  Used when
  *   n % 4 == 0 and n > block.  qrb200_workspace_bytes reflects the value set when it is called. */
 #define QRB200_OPT_CHART_BLOCK 5
-/*   QRB200_OPT_LU_BLOCK: column block of the two-level LU (0 = one level: every 32-wide panel
- *   updates the whole trailing matrix; 128 (default): the panels update only their block's
- *   columns and the rest of the trailing matrix takes one K = 128 update per block).  Used when
- *   the tcgen05 path is active and n > 128. */
-#define QRB200_OPT_LU_BLOCK 6
 int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return

@@ -23,7 +23,6 @@
 #include "qrb_tmap.cuh"
 #include "qrb_small.cuh"
 #include "qrb_warp.cuh"
-#include "qrb_lublk.cuh"
 
 #include <atomic>
 #include <type_traits>
@@ -99,8 +98,6 @@ constexpr int64_t kMaxChunk = 65535;              // grid.y / grid.z limit
 constexpr size_t kPanelSmemCap = 200 * 1024;
 // column block of the two-level Cholesky elimination (QRB200_OPT_CHOL_BLOCK; 0 = one level)
 static std::atomic<int> g_chol_block{128};
-// two-level LU (QRB200_OPT_LU_BLOCK: 0 = one level, 128 = blocks of 128 columns)
-static std::atomic<int> g_lu_block{128};
 
 // Panels taller than 512 rows run over a CTA cluster (qrb_panel_cl.cuh) when the rows are
 // float4-aligned, up to 4 x 512 rows, so those orders keep 32-wide panels too.
@@ -115,8 +112,8 @@ static int pick_nb(int n) {
 }
 
 static size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
-// Carving the workspace into per-lane parts costs at most 18 x 256 bytes of alignment each.
-constexpr size_t kLaneSlack = 4 * 18 * 256;
+// Carving the workspace into per-lane parts costs at most 13 x 256 bytes of alignment each.
+constexpr size_t kLaneSlack = 4 * 13 * 256;
 
 // Columns of the W / Wc panel buffers (rows of Bp): the panels of one Cholesky column block
 // keep theirs side by side when the two-level elimination runs (nb = 32, n > kCholBlock).
@@ -131,13 +128,9 @@ static int ws_cols(int n) {
   return c;
 }
 
-// two-level LU: one row-map slot per panel of a block (kLuBlock / kLuPanel) plus the composite
-constexpr int kLuSlots = kLuBlock / kLuPanel + 1;
-
 struct Ws {
   float *T0, *T1, *L, *R, *Q1, *W, *s, *mu, *D, *Wc, *Bp;
   int *orig, *srcmap;
-  int* lumaps;  // [kLuSlots][cb][n]
 };
 
 static size_t per_chunk_bytes(int64_t cb, int n, int nbmax) {
@@ -149,7 +142,6 @@ static size_t per_chunk_bytes(int64_t cb, int n, int nbmax) {
   t += align256(cb * sizeof(float));              // mu
   t += align256(cb * (size_t)n * sizeof(float));  // D
   t += 2 * align256(cb * (size_t)n * sizeof(int));
-  t += kLuSlots * align256(cb * (size_t)n * sizeof(int));  // two-level LU: row-map slots + map
   return t;
 }
 
@@ -179,8 +171,6 @@ static Ws carve(void* base, int64_t cb, int n, int nbmax) {
   w.D = (float*)take(cb * (size_t)n * sizeof(float));
   w.orig = (int*)take(cb * (size_t)n * sizeof(int));
   w.srcmap = (int*)take(cb * (size_t)n * sizeof(int));
-  w.lumaps = (int*)take(cb * (size_t)n * sizeof(int));
-  for (int i = 1; i < kLuSlots; ++i) take(cb * (size_t)n * sizeof(int));
   return w;
 }
 
@@ -313,10 +303,6 @@ static cudaError_t set_common_attrs() {
   if ((e = rwt_attr<RWTrail<float>>()) != cudaSuccess) return e;
   if ((e = rwt_attr<RWTrail<__nv_bfloat16>>()) != cudaSuccess) return e;
   if ((e = rwt_attr<RWTrail<__half>>()) != cudaSuccess) return e;
-  if ((e = cudaFuncSetAttribute(lu_blk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                (int)lu_prep_smem())) != cudaSuccess)
-    return e;
-  if ((e = tc_attr<WBlkTC>()) != cudaSuccess) return e;
   if ((e = small_attr<float>()) != cudaSuccess) return e;
   if ((e = small_attr<__nv_bfloat16>()) != cudaSuccess) return e;
   if ((e = small_attr<__half>()) != cudaSuccess) return e;
@@ -553,69 +539,7 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   if (e != cudaSuccess) return e;
 
   // ---- I-a: partial-pivot LU; P*L lands in ws.L ----
-  const bool lublk = tcp && rw && nb == kLuPanel && n > kLuBlock && g_lu_block.load() > 0;
-  if (lublk) {
-    // Two-level: the panels of a 128-column block update only the block's columns (with their
-    // own row maps, one slot per panel), then one K = 128 update covers the rest of the
-    // trailing matrix through the composite row map (qrb_lublk.cuh).
-    const void* cur = A;
-    bool cur_in = true;
-    float* Tb[2] = {ws.T0, ws.T1};
-    int ti = 0;
-    const int64_t sstride = (int64_t)(align256(cb * (size_t)n * sizeof(int)) / sizeof(int));
-    int* comp = ws.lumaps + (kLuSlots - 1) * sstride;
-    for (int kb = 0; kb < n; kb += kLuBlock) {
-      const int ke = (n - kb < kLuBlock) ? n : kb + kLuBlock;
-      const void* bs = cur;
-      const bool bs_in = cur_in;
-      int np = 0;
-      for (int k0 = kb; k0 < ke; k0 += nb, ++np) {
-        const int w = (n - k0 < nb) ? n - k0 : nb;
-        int* slot = ws.lumaps + np * sstride;
-        PanelArgs pa{};
-        pa.n = n; pa.k0 = k0; pa.w = w; pa.ldw = nb;
-        pa.src = cur; pa.orig = ws.orig; pa.srcmap = slot; pa.W = ws.W; pa.L = ws.L;
-        pa.info = info;
-        QRB_LAUNCH(prof, F_LU_PANEL,
-                   if (cur_in) launch_panel<PM_PIVOT, T, float>(pa, cb, st);
-                   else launch_panel<PM_PIVOT, float, float>(pa, cb, st));
-        const int k1 = k0 + w;
-        if (k1 < ke) {  // strip: the block's remaining columns, every row below the panel
-          RWTrailArgs rwa{n, k0, k1, nb, cur, Tb[ti], ws.W, slot, info};
-          rwa.ncol = ke;
-          QRB_LAUNCH(prof, F_LU_TRAIL,
-                     if (cur_in) tc::tc_rankw_kernel<RWTrail<T>>
-                         <<<rwt_grid(n - k1, ke - k1, cb), 256, tc::RWT_SMEM, st>>>(rwa);
-                     else tc::tc_rankw_kernel<RWTrail<float>>
-                         <<<rwt_grid(n - k1, ke - k1, cb), 256, tc::RWT_SMEM, st>>>(rwa));
-          cur = Tb[ti];
-          ti ^= 1;
-          cur_in = false;
-        }
-      }
-      if (ke < n) {
-        // the update goes to a buffer other than the block-start one, which it reads
-        float* out = (cur != bs) ? static_cast<float*>(const_cast<void*>(cur))
-                                 : (bs == ws.T0 ? ws.T1 : ws.T0);
-        const LuBlkArgs la{n, kb, ke, np, ws.lumaps, sstride, ws.orig, ws.L, comp, ws.Bp, info};
-        const WBlkArgs wa{n, kb, ke, kLuBlock, ws.orig, ws.L, ws.Bp, ws.W, info};
-        const tc::TrailWTCArgs ua{n, kb, ke, kLuBlock, bs, out, ws.W, comp, info};
-        QRB_LAUNCH(prof, F_LU_TRAIL,
-                   lu_blk_prep_kernel<<<(unsigned)cb, kLuPrepThreads, lu_prep_smem(), st>>>(la));
-        QRB_LAUNCH(prof, F_LU_TRAIL,
-                   tc::tc_gemm_kernel<WBlkTC, kTcBN><<<tc_grid(n - ke, ke - kb, cb), tc::NTHREADS,
-                                                       kTcSmem, st>>>(wa));
-        QRB_LAUNCH(prof, F_LU_TRAIL,
-                   if (bs_in) tc::tc_gemm_kernel<tc::TrailWTC<T>, kTcBN>
-                       <<<tc_grid(n - ke, n - ke, cb), tc::NTHREADS, kTcSmem, st>>>(ua);
-                   else tc::tc_gemm_kernel<tc::TrailWTC<float>, kTcBN>
-                       <<<tc_grid(n - ke, n - ke, cb), tc::NTHREADS, kTcSmem, st>>>(ua));
-        cur = out;
-        cur_in = false;
-        ti = (out == ws.T0) ? 1 : 0;
-      }
-    }
-  } else {
+  {
     const void* cur = A;
     bool cur_in = true;
     float* Tb[2] = {ws.T0, ws.T1};
@@ -951,11 +875,6 @@ int qrb200_set_option(int32_t key, int64_t value) {
   if (key == QRB200_OPT_CHOL_BLOCK) {
     if (value != 0 && value != 64 && value != 128 && value != 256) return QRB200_ERR_INVALID_ARG;
     qrb::g_chol_block.store((int)value);
-    return QRB200_OK;
-  }
-  if (key == QRB200_OPT_LU_BLOCK) {
-    if (value != 0 && value != qrb::kLuBlock) return QRB200_ERR_INVALID_ARG;
-    qrb::g_lu_block.store((int)value);
     return QRB200_OK;
   }
   if (key == QRB200_OPT_SMALL_N) {

@@ -118,15 +118,13 @@ struct RWTrailArgs {
   const float* W;
   const int* srcmap;  // nullptr -> identity
   int* info;
-  int ncol = 0;       // columns [k1, ncol) are updated (0 = n; the two-level LU's block strips)
 };
 template <typename T>
 struct RWTrail {
   using Args = RWTrailArgs;
   __device__ static int* info(const Args& a, int64_t b) { return a.info + b; }
   __device__ static void dims(const Args& a, int& M, int& N, int& K) {
-    M = a.n - a.k1;
-    N = (a.ncol > 0 ? a.ncol : a.n) - a.k1;
+    M = N = a.n - a.k1;
     K = a.k1 - a.k0;
   }
   __device__ static bool live(const Args&, int, int) { return true; }

@@ -39,7 +39,6 @@ OPT_SMALL_N = 2
 OPT_CHOL_BLOCK = 3
 OPT_LANES = 4
 OPT_CHART_BLOCK = 5
-OPT_LU_BLOCK = 6
 GEMM_AUTO, GEMM_SIMT, GEMM_TC = 0, 1, 2
 
 # every symbol include/qrb200.h declares, with its ctypes signature
@@ -180,12 +179,5 @@ def set_lanes(lanes: int) -> None:
 def set_chart_block(block: int) -> None:
     """Column block of the two-level chart elimination: 0 (one level), 64, 128 or 256."""
     rc = lib().qrb200_set_option(OPT_CHART_BLOCK, int(block))
-    if rc != QRB200_OK:
-        raise QRB200Error(rc, "qrb200_set_option")
-
-
-def set_lu_block(block: int) -> None:
-    """Column block of the two-level LU: 0 (one level) or 128."""
-    rc = lib().qrb200_set_option(OPT_LU_BLOCK, int(block))
     if rc != QRB200_OK:
         raise QRB200Error(rc, "qrb200_set_option")

@@ -488,27 +488,3 @@ def test_torch_operator_matches_entry_point(dtype):
     torch.cuda.synchronize()
     assert H.dtype == dtype and H.shape == A.shape and tau.shape == (3, 2, 96)
     assert torch.equal(H, H0) and torch.equal(tau, t0) and torch.equal(info, i0)
-
-
-@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("n", [160, 300, 512, 1040])
-def test_lu_block_levels(n, dtype):
-    """The two-level LU (QRB200_OPT_LU_BLOCK = 128: strips inside 128-column blocks, one
-    K = 128 update per block through the composite row map) against the one-level LU on the
-    same inputs: identical pivots (info, gates on all six classes) and tight agreement on the
-    dense matrices, including bf16 input read by the first block's update."""
-    from qrb200 import _lib, generators as G
-    A = G.heterogeneous(12, n, seed=97, device="cuda").to(dtype)
-    _lib.set_lu_block(0)
-    try:
-        H0, t0, i0 = qrb().geqrf(A)
-    finally:
-        _lib.set_lu_block(128)
-    H, tau, info = qrb().geqrf(A)
-    torch.cuda.synchronize()
-    assert torch.equal(info, i0) and int(info.abs().sum()) == 0
-    Af = A.float()
-    Hf, tf, _ = qrb().geqrf(Af)
-    assert_gates(Af, Hf, tf, f"two-level LU n={n}")
-    if dtype == torch.float32:
-        assert_tight(H[:2], tau[:2], H0[:2].cpu().numpy(), t0[:2].cpu().numpy())
