@@ -620,7 +620,9 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
       if (ke < n) {
         const RWGenArgs blk{n, ke, ke, n - ke, n - ke, ke - kb, kb, hblk, ws.T0, ws.W, info};
         QRB_LAUNCH(prof, F_CHART_TRAIL,
-                   rankw_kernel<RWGen><<<rw_grid(n - ke, n - ke, cb), 256, 0, st>>>(blk));
+                   rankw_big_kernel<RWGen><<<dim3((n - ke + RWB_T - 1) / RWB_T,
+                                                  (n - ke + RWB_T - 1) / RWB_T, (unsigned)cb),
+                                             256, 0, st>>>(blk));
       }
     }
   } else {

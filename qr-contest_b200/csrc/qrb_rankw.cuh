@@ -240,6 +240,99 @@ struct RWLinv {
   }
 };
 
+// ---- the same update for long K (the chart's K = 128 block update), SGEMM-shaped -----------
+// 128 x 128 output tile per CTA, 8 x 8 outputs per thread (rows ty*4 + i and 64 + ty*4 + i,
+// columns tx*4 + j and 64 + tx*4 + j, so a warp's shared-memory fragment reads are
+// conflict-free), K consumed in slices of 16 that are double-buffered: the global loads of
+// slice s+1 are in flight while slice s is multiplied out of shared memory.  Each output
+// accumulates its K products in order k = 0, 1, ... with fmaf, exactly like rankw_kernel, so
+// both give bit-identical results; this one issues ~4x fewer shared-memory loads per FMA.
+constexpr int RWB_T = 128, RWB_K = 16, RWB_LD = RWB_T + 4;
+
+template <class Pb>
+__global__ void __launch_bounds__(256, 2) rankw_big_kernel(typename Pb::Args a) {
+  __shared__ __align__(16) float As[2][RWB_K][RWB_LD];
+  __shared__ __align__(16) float Bs[2][RWB_K][RWB_LD];
+  const int64_t b = blockIdx.z;
+  const int m0 = blockIdx.y * RWB_T, n0 = blockIdx.x * RWB_T;
+  int M, N, K;
+  Pb::dims(a, M, N, K);
+  if (m0 >= M || n0 >= N || !Pb::live(a, m0, n0)) return;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  // loaders: A slice = 128 rows x 16 k (two float4 per thread), B slice = 16 k x 128 columns
+  const int am = tid >> 2, akc = tid & 3;        // rows am and am + 64, k 4*akc .. +3
+  const int bk = tid >> 5, bc = (tid & 31) * 4;  // k rows bk and bk + 8, columns bc .. +3
+  float4 ra[2], rb[2];
+  auto fetch = [&](int kb) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = am + 64 * h, k = kb + 4 * akc;
+      ra[h] = (m0 + m < M && k < K)
+                  ? __ldg(reinterpret_cast<const float4*>(Pb::a_ptr(a, b, m0 + m) + k))
+                  : make_float4(0.f, 0.f, 0.f, 0.f);
+      const int kk = kb + bk + 8 * h;
+      rb[h] = (kk < K && n0 + bc < N) ? ld4v(Pb::b_ptr(a, b, kk) + n0 + bc)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  auto put = [&](int buf) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int m = am + 64 * h;
+      As[buf][4 * akc + 0][m] = ra[h].x;
+      As[buf][4 * akc + 1][m] = ra[h].y;
+      As[buf][4 * akc + 2][m] = ra[h].z;
+      As[buf][4 * akc + 3][m] = ra[h].w;
+      st4(&Bs[buf][bk + 8 * h][bc], rb[h]);
+    }
+  };
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const int ns = (K + RWB_K - 1) / RWB_K;
+  fetch(0);
+  put(0);
+  __syncthreads();
+  for (int s = 0; s < ns; ++s) {
+    const int buf = s & 1;
+    if (s + 1 < ns) fetch((s + 1) * RWB_K);
+#pragma unroll
+    for (int k = 0; k < RWB_K; ++k) {
+      const float4 a0 = *reinterpret_cast<const float4*>(&As[buf][k][ty * 4]);
+      const float4 a1 = *reinterpret_cast<const float4*>(&As[buf][k][64 + ty * 4]);
+      const float4 b0 = *reinterpret_cast<const float4*>(&Bs[buf][k][tx * 4]);
+      const float4 b1 = *reinterpret_cast<const float4*>(&Bs[buf][k][64 + tx * 4]);
+      const float ar[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const float br[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
+    }
+    if (s + 1 < ns) {
+      put(buf ^ 1);  // the other buffer was last read in slice s - 1, before the barrier
+      __syncthreads();
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+    if (m >= M) continue;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = n0 + (h ? 64 : 0) + tx * 4;
+      if (j < N) {
+        float4 x = Pb::c_load4(a, b, m, j);
+        x.x -= acc[i][4 * h]; x.y -= acc[i][4 * h + 1];
+        x.z -= acc[i][4 * h + 2]; x.w -= acc[i][4 * h + 3];
+        Pb::store4(a, b, m, j, x);
+      }
+    }
+  }
+}
+
 // ---- general in-place rank-K update of a block of each matrix (K may exceed 32) ----------
 //   C[r0 + m][c0 + j] -= sum_k W[r0 + m][k] * C[kb + k][c0 + j],  m < M, j < N, k < K
 // W rows have ldw columns (the pointer already at the first column used).  The B rows
