@@ -138,6 +138,11 @@ struct RWTrail {
     return reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
            (int64_t)srow(a, b, a.k0 + k) * a.n + a.k1;
   }
+  // address of C_in at row m, column j (an L2 prefetch target), nullptr if it is never read
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    return reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
+           (int64_t)srow(a, b, a.k1 + m) * a.n + a.k1 + j;
+  }
   __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
     const T* c = reinterpret_cast<const T*>(a.Cold) + mat_off(b, a.n) +
                  (int64_t)srow(a, b, a.k1 + m) * a.n + a.k1 + j;
@@ -173,6 +178,10 @@ struct RWSyrk {
   }
   __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
     return a.R + mat_off(b, a.n) + (int64_t)(a.k0 + k) * a.n + a.k1;
+  }
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    if (j > m + 3) return nullptr;
+    return a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j;
   }
   __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
     if (j > m + 3) return make_float4(0.f, 0.f, 0.f, 0.f);  // strictly upper: never read
@@ -220,6 +229,11 @@ struct RWLinv {
   }
   // C_in: L_G^{-1}[r][j] for j < k0 on rows below the panel; 0 on the panel's own columns
   // (identity block) and on the panel rows, which are replaced outright (k0 % 4 == 0).
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    const int r = a.k0 + m;
+    if (r < a.k1 || j >= a.k0) return nullptr;
+    return a.RL + mat_off(b, a.n) + (int64_t)r * a.n + j;
+  }
   __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
     const int r = a.k0 + m;
     if (r < a.k1 || j >= a.k0) return make_float4(0.f, 0.f, 0.f, 0.f);

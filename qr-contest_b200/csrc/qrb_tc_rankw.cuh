@@ -46,6 +46,20 @@ __global__ void __launch_bounds__(NTHREADS, 3) tc_rankw_kernel(typename Pb::Args
     mbar_init(bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // Start the C tile on its way to L2 now: the epilogue's read of C (64 KB) then overlaps the
+  // operand loads, the split and the MMAs instead of following them.  Two 128-byte lines per
+  // thread: row tid / 2, lines (tid % 2) * 2 and +1 of the row's 512-byte segment.
+  {
+    const int row = tid >> 1;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = n0 + 32 * ((tid & 1) * 2 + h);
+      if (m0 + row < M && j < N) {
+        const void* p = Pb::c_addr(a, b, m0 + row, j);
+        if (p) asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+      }
+    }
+  }
   // A: micro-block (rows 4*mb.., k 4*kc..), rows contiguous in k
   {
     const int mb = tid >> 3, kc = tid & 7;
