@@ -49,6 +49,14 @@ __global__ void __launch_bounds__(256) rankw_kernel(typename Pb::Args a) {
   Pb::dims(a, M, N, K);
   if (m0 >= M || n0 >= N || !Pb::live(a, m0, n0)) return;
   const int tid = threadIdx.x;
+  // the C tile (64 rows x 4 lines of 128 bytes) starts towards L2 before the K loop
+  {
+    const int row = tid >> 2, j = n0 + 32 * (tid & 3);
+    if (m0 + row < M && j < N) {
+      const void* p = Pb::c_addr(a, b, m0 + row, j);
+      if (p) asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
+  }
 
   const int tn = tid & 15, tm = tid >> 4;
   float acc[4][8];
@@ -273,6 +281,15 @@ __global__ void __launch_bounds__(256, 2) rankw_big_kernel(typename Pb::Args a) 
   Pb::dims(a, M, N, K);
   if (m0 >= M || n0 >= N || !Pb::live(a, m0, n0)) return;
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  // the C tile (128 rows x 4 lines of 128 bytes) starts towards L2 before the K loop
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int idx = tid + 256 * h, row = idx >> 2, j = n0 + 32 * (idx & 3);
+    if (m0 + row < M && j < N) {
+      const void* p = Pb::c_addr(a, b, m0 + row, j);
+      if (p) asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
+  }
   // loaders: A slice = 128 rows x 16 k (two float4 per thread), B slice = 16 k x 128 columns
   const int am = tid >> 2, akc = tid & 3;        // rows am and am + 64, k 4*akc .. +3
   const int bk = tid >> 5, bc = (tid & 31) * 4;  // k rows bk and bk + 8, columns bc .. +3
@@ -372,6 +389,9 @@ struct RWGen {
   }
   __device__ static const float* b_ptr(const Args& a, int64_t b, int k) {
     return a.C + mat_off(b, a.n) + (int64_t)(a.kb + k) * a.n + a.c0;
+  }
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    return a.C + mat_off(b, a.n) + (int64_t)(a.r0 + m) * a.n + a.c0 + j;
   }
   __device__ static float4 c_load4(const Args& a, int64_t b, int m, int j) {
     return ld4rw(a.C + mat_off(b, a.n) + (int64_t)(a.r0 + m) * a.n + a.c0 + j);

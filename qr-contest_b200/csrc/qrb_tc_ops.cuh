@@ -81,6 +81,8 @@ struct GramTCArgs {
   int* info;
 };
 struct GramTC {
+  // the epilogue reads nothing from global memory (no early L2 prefetch)
+  __device__ static const void* c_addr(const GramTCArgs&, int64_t, int, int) { return nullptr; }
   using Args = GramTCArgs;
   static constexpr bool A_ALONG_K = false, B_ALONG_K = false;
   __device__ static void dims(const Args& a, int& M, int& N, int& K) { M = N = K = a.n; }
@@ -112,6 +114,7 @@ struct ClosureTCArgs {
 };
 template <typename T>
 struct ClosureTC {
+  __device__ static const void* c_addr(const ClosureTCArgs&, int64_t, int, int) { return nullptr; }
   using Args = ClosureTCArgs;
   static constexpr bool A_ALONG_K = false, B_ALONG_K = false;
   __device__ static void dims(const Args& a, int& M, int& N, int& K) { M = N = K = a.n; }
@@ -227,6 +230,10 @@ struct SyrkTC {
   __device__ static void loadB(const Args& a, int64_t b, int j0, int k0, float (&v)[4][4]) {
     loadA(a, b, j0, k0, v);
   }
+  // address the epilogue reads at (row m, column j) of the tile, for an early L2 prefetch
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    return a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j;
+  }
   __device__ static void store(const Args& a, int64_t b, int m, int j0, const float* v, int,
                                int N) {
     float* g = a.G + mat_off(b, a.n) + (int64_t)(a.k1 + m) * a.n + a.k1 + j0;
@@ -290,6 +297,9 @@ struct LinvBlkTC {
       for (int i = 0; i < 4; ++i)
         if (j0 + i >= jend) v[i][kk] = 0.f;
     }
+  }
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    return j < a.kb ? a.RL + mat_off(b, a.n) + (int64_t)(a.ke + m) * a.n + j : nullptr;
   }
   __device__ static void store(const Args& a, int64_t b, int m, int j0, const float* v, int,
                                int N) {
@@ -366,6 +376,9 @@ struct QApplyTC {
         v[i][kk] = r;
       }
     }
+  }
+  __device__ static const void* c_addr(const Args& a, int64_t b, int m, int j) {
+    return a.pass2 ? a.X + mat_off(b, a.n) + (int64_t)m * a.n + j : nullptr;
   }
   __device__ static void store(const Args& a, int64_t b, int m, int j0, const float* v, int,
                                int N) {

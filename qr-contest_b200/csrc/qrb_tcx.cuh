@@ -195,6 +195,15 @@ __global__ void __launch_bounds__(XTHREADS, C::MINB)
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
+  // Start the tile's epilogue reads (read-modify-write policies) on their way to L2 so that
+  // they overlap the main loop: 128 rows x 4 lines of 128 bytes.
+  for (int idx = tid; idx < BM * 4; idx += XTHREADS) {
+    const int row = idx >> 2, j = n0 + 32 * (idx & 3);
+    if (m0 + row < M && j < N) {
+      const void* p = Pb::c_addr(a, b, m0 + row, j);
+      if (p) asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+    }
+  }
   // per-column scale of the B transform (QApplyX: d_j^{-1/2}), read once per tile
   __shared__ __align__(16) float tscale[BN];
   if constexpr (Pb::TILE_SCALE)
