@@ -497,6 +497,17 @@ def measure_c5(dev, rank, world):
     ms = dev_time(step, dev, reps=2, warm=1, world=world)
     H, tau, info = out["r"]
     del ws
+    # per-family CUDA-event timings of the library on the first 8192 matrices of the shard
+    from qrb200 import _lib
+    bs = min(b, 8192)
+    As = A[:bs].contiguous()
+    wss = torch.empty(qrb200.api.workspace_bytes(bs, n), dtype=torch.uint8, device=dev)
+    Hh, th = torch.empty_like(As), torch.empty(bs, n, dtype=As.dtype, device=dev)
+    inf = torch.zeros(bs, dtype=torch.int32, device=dev)
+    _, fam = _lib.geqrf_batched_timed(As.data_ptr(), Hh.data_ptr(), th.data_ptr(), inf.data_ptr(),
+                                      bs, n, _lib.QRB200_BF16, wss.data_ptr(), wss.numel(),
+                                      torch.cuda.current_stream(dev).cuda_stream)
+    del As, wss, Hh, th, inf
     bad = int((info != 0).sum())
     # float32 factors of a sample of this shard's (bf16) inputs, gated in float64
     As = A[:96].float()
@@ -507,7 +518,8 @@ def measure_c5(dev, rank, world):
          "matrices_per_s": gb / (ms / 1e3), "tflops_7n3": gb / (ms / 1e3) * algo_flops(n) / 1e12,
          "tensor_frac_per_gpu": gb / world / (ms / 1e3) * algo_flops(n) / 1e12 / (bf16 / 6),
          "info_nonzero_rank0": bad, "gates_rank0_sample96_fp32": gates,
-         "scaling": "strong (fixed global batch)"}
+         "scaling": "strong (fixed global batch)",
+         "family_ms_first_8192": {k: round(v, 3) for k, v in fam.items() if v > 0}}
     if world > 1:
         import torch.distributed as dist
         Hall = torch.empty(gb, n, n, dtype=H.dtype, device=dev)

@@ -145,6 +145,11 @@ long long qrb200_launch_count(void);
  *   the rest of the trailing matrix takes one float32 K = block update per block.  Used when
  *   n % 4 == 0 and n > block.  qrb200_workspace_bytes reflects the value set when it is called. */
 #define QRB200_OPT_CHART_BLOCK 5
+/*   QRB200_OPT_PANEL_LOOP: column loop of the register-resident panels (panels of at most 512
+ *   rows): 0 = automatic (default), 1 = fully unrolled, 2 = rotating registers (one column
+ *   step of code, smaller than the instruction cache).  Both loops give bit-identical
+ *   results. */
+#define QRB200_OPT_PANEL_LOOP 6
 int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return

@@ -368,12 +368,29 @@ static cudaError_t ensure_attrs() {
 
 // Panels of at most 512 rows run register-resident (qrb_panel_reg.cuh); taller panels keep
 // the shared-memory panel kernel.
+// QRB200_OPT_PANEL_LOOP: 0 automatic, 1 unrolled column loop everywhere, 2 rotating loop
+static std::atomic<int> g_panel_loop{0};
 template <int MODE, typename TIn, typename TOut>
 static void launch_panel(const PanelArgs& pa, int64_t cb, cudaStream_t st) {
   const int m = pa.n - pa.k0;
-  if (m <= 128) panel_reg_kernel<MODE, TIn, TOut, 1, 128><<<(unsigned)cb, 128, 0, st>>>(pa);
-  else if (m <= 256) panel_reg_kernel<MODE, TIn, TOut, 1><<<(unsigned)cb, 256, 0, st>>>(pa);
-  else if (m <= 512) panel_reg_kernel<MODE, TIn, TOut, 2><<<(unsigned)cb, 256, 0, st>>>(pa);
+  const int pl = g_panel_loop.load(std::memory_order_relaxed);
+  // automatic: the rotating (not unrolled) column loop for two rows per thread, whose
+  // unrolled code overflows the instruction cache, and for LU panels; Cholesky and chart
+  // panels of one row per thread keep the unrolled loop (exact update ranges: about half the
+  // FMAs).  Measured per 1536 matrices at n = 512 (rotating vs unrolled): lu_panel 3.26 vs
+  // 4.17 ms, chol_panel 4.86 vs 6.04, chart_panel 2.37 vs 2.63; per 8192 bf16 matrices at
+  // n = 256: lu_panel 4.62 vs 4.78, chol_panel 6.44 vs 5.88, chart_panel 3.31 vs 3.04.
+  const bool rot1 = pl == 2 || (pl == 0 && MODE == PM_PIVOT), rot2 = pl != 1;
+  if (m <= 128) {
+    if (rot1) panel_reg_kernel<MODE, TIn, TOut, 1, 128, true><<<(unsigned)cb, 128, 0, st>>>(pa);
+    else panel_reg_kernel<MODE, TIn, TOut, 1, 128, false><<<(unsigned)cb, 128, 0, st>>>(pa);
+  } else if (m <= 256) {
+    if (rot1) panel_reg_kernel<MODE, TIn, TOut, 1, 256, true><<<(unsigned)cb, 256, 0, st>>>(pa);
+    else panel_reg_kernel<MODE, TIn, TOut, 1, 256, false><<<(unsigned)cb, 256, 0, st>>>(pa);
+  } else if (m <= 512) {
+    if (rot2) panel_reg_kernel<MODE, TIn, TOut, 2, 256, true><<<(unsigned)cb, 256, 0, st>>>(pa);
+    else panel_reg_kernel<MODE, TIn, TOut, 2, 256, false><<<(unsigned)cb, 256, 0, st>>>(pa);
+  }
   else if (cluster_panel(pa.n) && m <= 2 * kClRows)
     panel_cl_kernel<MODE, TIn, TOut, 2><<<(unsigned)(2 * cb), 256, 0, st>>>(pa);
   else if (cluster_panel(pa.n))
@@ -877,6 +894,11 @@ int qrb200_set_option(int32_t key, int64_t value) {
   if (key == QRB200_OPT_CHOL_BLOCK) {
     if (value != 0 && value != 64 && value != 128 && value != 256) return QRB200_ERR_INVALID_ARG;
     qrb::g_chol_block.store((int)value);
+    return QRB200_OK;
+  }
+  if (key == QRB200_OPT_PANEL_LOOP) {
+    if (value < 0 || value > 2) return QRB200_ERR_INVALID_ARG;
+    qrb::g_panel_loop.store((int)value);
     return QRB200_OK;
   }
   if (key == QRB200_OPT_SMALL_N) {

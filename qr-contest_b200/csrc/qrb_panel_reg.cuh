@@ -67,9 +67,21 @@ __device__ __forceinline__ void times_l11_inv(float (&x)[PR_W], const float (*Ls
   }
 }
 
+// x[q][i] <- x[q][i + 1], x[q][31] <- x[q][0] for every row (register moves only)
+template <int RPT>
+__device__ __forceinline__ void rotate_left(float (&x)[RPT][PR_W]) {
+#pragma unroll
+  for (int q = 0; q < RPT; ++q) {
+    const float t = x[q][0];
+#pragma unroll
+    for (int i = 0; i < PR_W - 1; ++i) x[q][i] = x[q][i + 1];
+    x[q][PR_W - 1] = t;
+  }
+}
+
 // NT threads per CTA (256; 128 for panels of at most 128 rows, which then fit twice as many
 // CTAs per SM).
-template <int MODE, typename TIn, typename TOut, int RPT, int NT = 256>
+template <int MODE, typename TIn, typename TOut, int RPT, int NT = 256, bool ROT = true>
 __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
     panel_reg_kernel(PanelArgs a) {
   constexpr int NWARP = NT / 32;
@@ -77,7 +89,7 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
   const int64_t b = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
 
-  __shared__ float prow[2][PR_W];
+  __shared__ __align__(16) float prow[2][PR_W];
   __shared__ float Ls[PR_W][PR_W + 1];   // multipliers of the pivot rows, by position
   __shared__ float dpiv[PR_W];
   __shared__ float red_v[2][NWARP];
@@ -129,7 +141,158 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
   __syncthreads();
 
   QRB_PT(1);
+  if constexpr (ROT) {
   // ---- column-by-column elimination ----
+  // The column loop is NOT unrolled: fully unrolled, 32 column steps of straight-line code
+  // overflow the instruction cache (ncu: "no instruction" was the top stall, 9 cycles per issue,
+  // with issue slots 12 % busy).  To keep register indices compile-time constants in a runtime
+  // loop, every row rotates its registers left by one in each step: before step c, x[q][i]
+  // holds column c + i for i < 32 - c and the finished multiplier of column i - (32 - c) for
+  // i >= 32 - c, so the pivot column is always x[q][0].  The pivot row is published in the
+  // same rotated order (prow[i] = column c + i, zero past the panel), so one branch-free pass
+  // x[i-1] <- x[i] - l prow[i] both updates and rotates a row; rows that take no update use
+  // l = 0 (adding -0 * prow leaves them unchanged).  After 32 rotations (the w steps, then
+  // 32 - w idle ones) every value is back at its column.
+#pragma unroll 1
+  for (int c = 0; c < w; ++c) {
+    const int par = c & 1;
+    const int nr = PR_W - c;  // registers [0, nr) hold the live columns c .. 31
+    float4* pr4 = reinterpret_cast<float4*>(prow[par]);
+    bool upd[RPT];
+    float l[RPT];
+    if (MODE == PM_PIVOT) {
+      // candidate key: |a| bits (monotone for non-negative floats; NaN counts as 0 and is
+      // flagged), then the lowest current position.  Warp reductions with redux.sync.
+      unsigned bv = 0u;
+      int bp = INT_MAX, br = -1;
+      bool bad = false;
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        if (live[q]) {
+          const int r = tid + NT * q;
+          const float xv = x[q][0];
+          bad |= !isfinite(xv);
+          const unsigned v = isnan(xv) ? 0u : __float_as_uint(fabsf(xv));
+          const int p = rowpos[r];
+          if (v > bv || (v == bv && p < bp)) { bv = v; bp = p; br = r; }
+        }
+      }
+      if (bad) atomicOr(&s_flags, INFO_NONFINITE_INPUT);
+      const unsigned wv = __reduce_max_sync(0xffffffffu, bv);
+      const int wp = (int)__reduce_min_sync(0xffffffffu, (bv == wv) ? (unsigned)bp : 0xffffffffu);
+      const unsigned own = __ballot_sync(0xffffffffu, bv == wv && bp == wp);
+      const int wr = __shfl_sync(0xffffffffu, br, own ? (__ffs(own) - 1) : 0);
+      if (lane == 0) {
+        red_v[par][warp] = __uint_as_float(wv);
+        red_p[par][warp] = wp;
+        red_r[par][warp] = wr;
+      }
+      __syncthreads();
+      unsigned V = __float_as_uint(red_v[par][0]);
+      int Pp = red_p[par][0], Rw = red_r[par][0];
+#pragma unroll
+      for (int i = 1; i < NWARP; ++i) {
+        const unsigned vi = __float_as_uint(red_v[par][i]);
+        const int pi = red_p[par][i];
+        if (vi > V || (vi == V && pi < Pp)) { V = vi; Pp = pi; Rw = red_r[par][i]; }
+      }
+      // the winner publishes its row (U row c, rotated, and its multipliers for columns < c)
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        if (tid + NT * q == Rw) {
+#pragma unroll
+          for (int i = 0; i < PR_W; i += 4)
+            pr4[i / 4] = make_float4((c + i < w) ? x[q][i] : 0.f, (c + i + 1 < w) ? x[q][i + 1] : 0.f,
+                                     (c + i + 2 < w) ? x[q][i + 2] : 0.f,
+                                     (c + i + 3 < w) ? x[q][i + 3] : 0.f);
+#pragma unroll
+          for (int i = 1; i < PR_W; ++i)
+            if (i >= nr) Ls[c][i - nr] = x[q][i];
+          live[q] = false;
+        }
+      }
+      if (tid == 0 && Pp != c) {  // replay getrf's swap of positions c and Pp
+        const int rc = posrow[c];
+        posrow[c] = Rw; posrow[Pp] = rc;
+        rowpos[Rw] = c; rowpos[rc] = Pp;
+      }
+      __syncthreads();
+      const float pv = prow[par][0];
+      const float scale = (pv != 0.f) ? 1.f / pv : 1.f;
+      if (tid == 0) {
+        dpiv[c] = pv;
+        if (pv == 0.f) atomicOr(&s_flags, INFO_LU_ZERO_PIVOT);
+      }
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        upd[q] = live[q];
+        l[q] = upd[q] ? x[q][0] * scale : 0.f;
+      }
+    } else {
+      // row c is the pivot row (no pivoting); rows c .. w-1 live in threads c .. w-1, q = 0
+      if (MODE == PM_CHOL) {
+        if (tid >= c && tid < w) prow[par][tid - c] = x[0][0];  // U[c][j] = S[j][c]
+        if (tid >= w - c && tid < PR_W) prow[par][tid] = 0.f;
+      } else {
+        if (tid == c) {
+#pragma unroll
+          for (int i = 0; i < PR_W; i += 4)
+            pr4[i / 4] = make_float4((c + i < w) ? x[0][i] : 0.f, (c + i + 1 < w) ? x[0][i + 1] : 0.f,
+                                     (c + i + 2 < w) ? x[0][i + 2] : 0.f,
+                                     (c + i + 3 < w) ? x[0][i + 3] : 0.f);
+        }
+      }
+      if (tid == c) {
+#pragma unroll
+        for (int i = 1; i < PR_W; ++i)
+          if (i >= nr) Ls[c][i - nr] = x[0][i];
+      }
+      __syncthreads();
+      // CHOL: the jitter enters with the diagonal entry when it becomes the pivot (adding it
+      // before or after the earlier updates of that entry differs only by rounding)
+      const float pv = prow[par][0] + ((MODE == PM_CHOL) ? s_mu : 0.f);
+      float piv = pv, sgn = 1.f, rpiv = 1.f;
+      if (MODE == PM_CHOL) {
+        if (!(pv > 0.f)) {
+          if (tid == 0) atomicOr(&s_flags, a.info_bit);
+          piv = 1.f;  // keep the arithmetic finite; the host reports the failure
+        }
+        rpiv = __frcp_rn(piv);
+        if (tid == 0) dpiv[c] = piv;
+      } else {
+        const float pp = 1.f - pv, pm = 1.f + pv;
+        sgn = (fabsf(pp) >= fabsf(pm)) ? 1.f : -1.f;
+        piv = (sgn > 0.f) ? pp : pm;
+        if (tid == 0) dpiv[c] = sgn;
+      }
+#pragma unroll
+      for (int q = 0; q < RPT; ++q) {
+        const int r = tid + NT * q;
+        upd[q] = r > c && r < m;
+        // Cholesky scales by the reciprocal pivot (as potf2 does); the chart divides (:158)
+        l[q] = !upd[q] ? 0.f : (MODE == PM_CHOL) ? x[q][0] * rpiv : (-sgn * x[q][0]) / piv;
+      }
+    }
+    // update and rotate: x[i-1] <- x[i] - l prow[i] (i = 1..31), x[31] <- l or the kept value
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {
+      const float x0 = x[q][0];
+#pragma unroll
+      for (int i4 = 0; i4 < PR_W / 4; ++i4) {
+        const float4 p4 = pr4[i4];
+        const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int i = 4 * i4 + u;
+          if (i >= 1) x[q][i - 1] = fmaf(-l[q], pp[u], x[q][i]);
+        }
+      }
+      x[q][PR_W - 1] = upd[q] ? l[q] : x0;
+    }
+  }
+  for (int c = w; c < PR_W; ++c) rotate_left(x);
+  } else {
+  // fully unrolled column loop (32 straight-line column steps, exact update ranges)
 #pragma unroll
   for (int c = 0; c < PR_W; ++c) {
     if (c >= w) break;
@@ -251,6 +414,7 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
         }
       }
     }
+  }
   }
   __syncthreads();
 

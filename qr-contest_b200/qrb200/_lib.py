@@ -39,6 +39,7 @@ OPT_SMALL_N = 2
 OPT_CHOL_BLOCK = 3
 OPT_LANES = 4
 OPT_CHART_BLOCK = 5
+OPT_PANEL_LOOP = 6
 GEMM_AUTO, GEMM_SIMT, GEMM_TC = 0, 1, 2
 
 # every symbol include/qrb200.h declares, with its ctypes signature
@@ -180,4 +181,11 @@ def set_chart_block(block: int) -> None:
     """Column block of the two-level chart elimination: 0 (one level), 64, 128 or 256."""
     rc = lib().qrb200_set_option(OPT_CHART_BLOCK, int(block))
     if rc != QRB200_OK:
+        raise QRB200Error(rc, "qrb200_set_option")
+
+
+def set_panel_loop(mode: int) -> None:
+    """Column loop of the register-resident panels: 0 automatic, 1 unrolled, 2 rotating."""
+    rc = lib().qrb200_set_option(OPT_PANEL_LOOP, int(mode))
+    if rc != 0:
         raise QRB200Error(rc, "qrb200_set_option")

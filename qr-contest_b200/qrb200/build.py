@@ -77,11 +77,16 @@ def _compile_ops(verbose: bool) -> None:
 
 
 def build(force: bool = False, verbose: bool = False, extra=()) -> Path:
-    for src, out, defs in ((CSRC / "qrb_api.cu", LIB, []),
-                           (CSRC / "qrb_api.cu", CHECKED, ["-DQRB_BOUNDS_CHECK"]),
-                           (CSRC / "qrb_testkit.cu", TESTKIT, ["-DQRB_PANEL_TIMERS"])):
-        if force or not up_to_date(out):
-            _compile(src, out, verbose, [*extra, *defs])
+    # the three nvcc runs are independent (minutes each): run them side by side
+    from concurrent.futures import ThreadPoolExecutor
+    jobs = [(src, out, defs) for src, out, defs in
+            ((CSRC / "qrb_api.cu", LIB, []),
+             (CSRC / "qrb_api.cu", CHECKED, ["-DQRB_BOUNDS_CHECK"]),
+             (CSRC / "qrb_testkit.cu", TESTKIT, ["-DQRB_PANEL_TIMERS"]))
+            if force or not up_to_date(out)]
+    with ThreadPoolExecutor(max_workers=max(1, len(jobs))) as ex:
+        for f in [ex.submit(_compile, src, out, verbose, [*extra, *defs]) for src, out, defs in jobs]:
+            f.result()
     if force or not up_to_date(OPS) or OPS.stat().st_mtime < (CSRC / "qrb_torch_op.cpp").stat().st_mtime:
         _compile_ops(verbose)
     return LIB

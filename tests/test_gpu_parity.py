@@ -281,6 +281,24 @@ def test_lanes_bit_identical(lanes):
     assert torch.equal(tau, t0) and torch.equal(info, i0)
 
 
+@pytest.mark.parametrize("n", [66, 100, 130, 257, 384, 512])
+def test_panel_loops_bit_identical(n):
+    """The register panels' two column loops (fully unrolled; rotating registers) perform the
+    same floating-point operations in the same order, so H, tau and info agree bit for bit
+    (LU, Cholesky and chart panels; the last panel narrower than 32 when n % 32 != 0)."""
+    from qrb200 import _lib, generators as G
+    A = G.heterogeneous(18, n, seed=53, device="cuda")
+    outs = []
+    try:
+        for mode in (1, 2):
+            _lib.set_panel_loop(mode)
+            outs.append(qrb().geqrf(A))
+    finally:
+        _lib.set_panel_loop(0)
+    (H1, t1, i1), (H2, t2, i2) = outs
+    assert torch.equal(H1, H2) and torch.equal(t1, t2) and torch.equal(i1, i2)
+
+
 @pytest.mark.parametrize("block", [0, 64, 256])
 @pytest.mark.parametrize("n", [192, 320, 512])
 def test_chart_block_widths(block, n):
