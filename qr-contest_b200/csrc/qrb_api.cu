@@ -310,6 +310,8 @@ static cudaError_t set_common_attrs() {
   if ((e = tcx_attr<tcx::SyrkX>()) != cudaSuccess) return e;
   if ((e = tcx_attr<tcx::LinvBlkX>()) != cudaSuccess) return e;
   if ((e = tcx_attr<tcx::QApplyX>()) != cudaSuccess) return e;
+  if ((e = tcx_attr<tcx::ClosureXT<__nv_bfloat16>>()) != cudaSuccess) return e;
+  if ((e = tcx_attr<tcx::ClosureXT<__half>>()) != cudaSuccess) return e;
   return tcx_attr<tcx::ClosureX>();
 }
 
@@ -514,6 +516,18 @@ static void launch_small(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
 
 // Explicit Q (optional output): householder_product(H, tau) = (I - Y T Y^T) = Q_frame * S,
 // because the chart factors I - Q_frame S = Y (T Y^T) (reflection_no_reflectors.py:86-176).
+// 16-bit input widened to float32 (n % 4 == 0: four elements per thread and step), the B
+// operand of the TMA-fed closure tile.
+template <typename T>
+__global__ void widen_kernel(const T* __restrict__ A, float* __restrict__ X, int64_t count4) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < count4;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const uint2 t = __ldg(reinterpret_cast<const uint2*>(A) + q);
+    const T* h = reinterpret_cast<const T*>(&t);
+    reinterpret_cast<float4*>(X)[q] = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+  }
+}
+
 // One float4 of Q per thread: Q[r][c] = frame[r][c] * s_c, in the output dtype.
 template <typename T>
 __global__ void explicit_q_kernel(const float* __restrict__ F, const float* __restrict__ s,
@@ -661,12 +675,22 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
     }
   }
   // ---- II: closure, H_upper = s * triu(Q^T A) ----
+  // float32 input: A is the closure tile's B operand; 16-bit input is widened into ws.T1 (free
+  // after the LU) first, so that the TMA-fed tile serves every dtype (measured at n = 256, 8192
+  // bf16 matrices: closure 7.3 ms on the register-fed tile)
   tcx::Maps cm;
-  const bool cx = tcp && std::is_same<T, float>::value && tcx_maps(cm, ws.L, false, A, false, n, cb);
+  constexpr bool f32 = std::is_same<T, float>::value;
+  const bool cx = tcp && (f32 || (reinterpret_cast<uintptr_t>(A) & 7) == 0) &&
+                  tcx_maps(cm, ws.L, false, f32 ? static_cast<const void*>(A) : ws.T1, false, n, cb);
+  if (cx && !f32) {
+    const int64_t c4 = cb * (int64_t)n * n / 4;
+    const unsigned gw = (unsigned)((c4 + 255) / 256 < 148 * 16 ? (c4 + 255) / 256 : 148 * 16);
+    QRB_LAUNCH(prof, F_CLOSURE, (widen_kernel<T><<<gw, 256, 0, st>>>(A, ws.T1, c4)));
+  }
   QRB_LAUNCH(prof, F_CLOSURE,
              // the closure keeps the one-CTA shape at every K: its epilogue waits on global
              // loads of A, and two CTAs per SM measured slower (2.51 -> 2.59 ms, n = 512)
-             if (cx) launch_tcx<tcx::ClosureX>(tc_grid(n, n, cb), cm,
+             if (cx) launch_tcx<tcx::ClosureXT<T>>(tc_grid(n, n, cb), cm,
                                                tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info},
                                                tcx::kDualMaxK + 1, st);
              else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>

@@ -13,6 +13,8 @@
 //   PM_CHART : the owner of row c publishes it; 1 barrier per column.
 // W = L21 L11^{-1} and L11^{-1} are computed in registers (right-looking substitution).
 #pragma once
+#include <type_traits>
+
 #include "qrb_panel.cuh"
 
 namespace qrb {
@@ -77,6 +79,19 @@ __device__ __forceinline__ void rotate_left(float (&x)[RPT][PR_W]) {
     for (int i = 0; i < PR_W - 1; ++i) x[q][i] = x[q][i + 1];
     x[q][PR_W - 1] = t;
   }
+}
+
+// The finished multipliers a pivot row holds, by column (Ls[j] = multiplier of column j < c),
+// from a row's registers in the rotated layout of the column loop (see panel_reg_kernel).
+template <int RING>
+__device__ __forceinline__ void publish_multipliers(const float (&xr)[PR_W], float* Ls_c, int nr) {
+  if constexpr (RING == 16) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) Ls_c[j] = xr[16 + j];
+  }
+#pragma unroll
+  for (int i = 1; i < RING; ++i)
+    if (i >= nr) Ls_c[i - nr + (PR_W - RING)] = xr[i];
 }
 
 // NT threads per CTA (256; 128 for panels of at most 128 rows, which then fit twice as many
@@ -146,17 +161,21 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
   // The column loop is NOT unrolled: fully unrolled, 32 column steps of straight-line code
   // overflow the instruction cache (ncu: "no instruction" was the top stall, 9 cycles per issue,
   // with issue slots 12 % busy).  To keep register indices compile-time constants in a runtime
-  // loop, every row rotates its registers left by one in each step: before step c, x[q][i]
-  // holds column c + i for i < 32 - c and the finished multiplier of column i - (32 - c) for
-  // i >= 32 - c, so the pivot column is always x[q][0].  The pivot row is published in the
-  // same rotated order (prow[i] = column c + i, zero past the panel), so one branch-free pass
-  // x[i-1] <- x[i] - l prow[i] both updates and rotates a row; rows that take no update use
-  // l = 0 (adding -0 * prow leaves them unchanged).  After 32 rotations (the w steps, then
-  // 32 - w idle ones) every value is back at its column.
-#pragma unroll 1
-  for (int c = 0; c < w; ++c) {
+  // loop, every row rotates a ring of its registers left by one in each step, so the pivot
+  // column is always x[q][0].  Full-width panels use a 32-register ring for columns 0-15
+  // (before step c, x[q][i] holds column c + i for i < 32 - c and the finished multiplier of
+  // column i - (32 - c) above that) and a 16-register ring for columns 16-31 (the multipliers
+  // of columns 0-15 rest in x[q][16..31]; before step c, x[q][i] holds column c + i for
+  // i < 32 - c and the multiplier of column i + c - 16 for 32 - c <= i < 16), which halves the
+  // update work of the second half.  The pivot row is published in the same rotated order
+  // (prow[i] = column c + i, zero past the panel), so one branch-free pass
+  // x[i-1] <- x[i] - l prow[i] both updates and rotates a ring; rows that take no update use
+  // l = 0 (adding -0 * prow leaves them unchanged).  Narrower panels use the 32-register ring
+  // for all w steps and 32 - w idle rotations.  At the end every value is back at its column.
+  auto col_step = [&](const int c, auto ring_c) {
+    constexpr int RING = decltype(ring_c)::value;  // 32 or 16 registers rotate
     const int par = c & 1;
-    const int nr = PR_W - c;  // registers [0, nr) hold the live columns c .. 31
+    const int nr = PR_W - c;  // ring positions [0, nr) hold the live columns c .. 31
     float4* pr4 = reinterpret_cast<float4*>(prow[par]);
     bool upd[RPT];
     float l[RPT];
@@ -201,13 +220,11 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
       for (int q = 0; q < RPT; ++q) {
         if (tid + NT * q == Rw) {
 #pragma unroll
-          for (int i = 0; i < PR_W; i += 4)
+          for (int i = 0; i < RING; i += 4)
             pr4[i / 4] = make_float4((c + i < w) ? x[q][i] : 0.f, (c + i + 1 < w) ? x[q][i + 1] : 0.f,
                                      (c + i + 2 < w) ? x[q][i + 2] : 0.f,
                                      (c + i + 3 < w) ? x[q][i + 3] : 0.f);
-#pragma unroll
-          for (int i = 1; i < PR_W; ++i)
-            if (i >= nr) Ls[c][i - nr] = x[q][i];
+          publish_multipliers<RING>(x[q], Ls[c], nr);
           live[q] = false;
         }
       }
@@ -236,16 +253,14 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
       } else {
         if (tid == c) {
 #pragma unroll
-          for (int i = 0; i < PR_W; i += 4)
+          for (int i = 0; i < RING; i += 4)
             pr4[i / 4] = make_float4((c + i < w) ? x[0][i] : 0.f, (c + i + 1 < w) ? x[0][i + 1] : 0.f,
                                      (c + i + 2 < w) ? x[0][i + 2] : 0.f,
                                      (c + i + 3 < w) ? x[0][i + 3] : 0.f);
         }
       }
       if (tid == c) {
-#pragma unroll
-        for (int i = 1; i < PR_W; ++i)
-          if (i >= nr) Ls[c][i - nr] = x[0][i];
+        publish_multipliers<RING>(x[0], Ls[c], nr);
       }
       __syncthreads();
       // CHOL: the jitter enters with the diagonal entry when it becomes the pivot (adding it
@@ -278,7 +293,7 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
     for (int q = 0; q < RPT; ++q) {
       const float x0 = x[q][0];
 #pragma unroll
-      for (int i4 = 0; i4 < PR_W / 4; ++i4) {
+      for (int i4 = 0; i4 < RING / 4; ++i4) {
         const float4 p4 = pr4[i4];
         const float pp[4] = {p4.x, p4.y, p4.z, p4.w};
 #pragma unroll
@@ -287,10 +302,30 @@ __global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : 2))
           if (i >= 1) x[q][i - 1] = fmaf(-l[q], pp[u], x[q][i]);
         }
       }
-      x[q][PR_W - 1] = upd[q] ? l[q] : x0;
+      x[q][RING - 1] = upd[q] ? l[q] : x0;
     }
+  };
+  using Ring32 = std::integral_constant<int, 32>;
+  using Ring16 = std::integral_constant<int, 16>;
+  if (w == PR_W) {
+#pragma unroll 1
+    for (int c = 0; c < 16; ++c) col_step(c, Ring32{});
+#pragma unroll 1
+    for (int c = 16; c < PR_W; ++c) col_step(c, Ring16{});
+#pragma unroll
+    for (int q = 0; q < RPT; ++q) {  // x[q][i] holds column 16 + i, x[q][16 + i] column i
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float t = x[q][i];
+        x[q][i] = x[q][16 + i];
+        x[q][16 + i] = t;
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < w; ++c) col_step(c, Ring32{});
+    for (int c = w; c < PR_W; ++c) rotate_left(x);
   }
-  for (int c = w; c < PR_W; ++c) rotate_left(x);
   } else {
   // fully unrolled column loop (32 straight-line column steps, exact update ranges)
 #pragma unroll

@@ -451,12 +451,17 @@ struct QApplyX : tc::QApplyTC {
     }
   }
 };
-struct ClosureX : tc::ClosureTC<float> {
+// T = the output dtype; B (A of the factorization) is always read as float32 (a 16-bit input
+// is widened into the workspace first, as the reference's .to(float32) does)
+template <typename T>
+struct ClosureXT : tc::ClosureTC<T> {
+  using Args = typename tc::ClosureTC<T>::Args;
   static constexpr bool A_KMAJOR = false, B_KMAJOR = false;  // Q[k][m], A[k][j]
   static constexpr bool A_TMEM = true;
   __device__ static void org(const Args&, int& ar, int& ak, int& br, int& bk) { ar = ak = br = bk = 0; }
   static constexpr bool TILE_SCALE = false;
 };
+using ClosureX = ClosureXT<float>;
 
 // K = block updates of the two-level Cholesky elimination (see SyrkTC / LinvBlkTC in
 // qrb_tc_ops.cuh) on the TMA-fed tile.  org() places the operand tiles inside the mapped
