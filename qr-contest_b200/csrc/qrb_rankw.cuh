@@ -101,6 +101,18 @@ __global__ void __launch_bounds__(256) rankw_kernel(typename Pb::Args a) {
         for (int j = 0; j < 8; ++j) acc[i][j] = fmaf(ar[i], br[j], acc[i][j]);
     }
   }
+  // all C loads of the thread first, then the stores (C may be updated in place: a load after
+  // a store would wait for its own round trip)
+  float4 xs[4][2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + tm * 4 + i;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int j = n0 + tn * 8 + 4 * h;
+      if (m < M && j < N) xs[i][h] = Pb::c_load4(a, b, m, j);
+    }
+  }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int m = m0 + tm * 4 + i;
@@ -109,7 +121,7 @@ __global__ void __launch_bounds__(256) rankw_kernel(typename Pb::Args a) {
     for (int h = 0; h < 2; ++h) {
       const int j = n0 + tn * 8 + 4 * h;
       if (j < N) {
-        float4 x = Pb::c_load4(a, b, m, j);
+        float4 x = xs[i][h];
         x.x -= acc[i][4 * h]; x.y -= acc[i][4 * h + 1];
         x.z -= acc[i][4 * h + 2]; x.w -= acc[i][4 * h + 3];
         Pb::store4(a, b, m, j, x);
@@ -347,18 +359,32 @@ __global__ void __launch_bounds__(256, 2) rankw_big_kernel(typename Pb::Args a) 
       __syncthreads();
     }
   }
+  // C loads of four rows issued before their stores (C may be updated in place)
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
-    if (m >= M) continue;
+  for (int i0 = 0; i0 < 8; i0 += 4) {
+    float4 xs[4][2];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int j = n0 + (h ? 64 : 0) + tx * 4;
-      if (j < N) {
-        float4 x = Pb::c_load4(a, b, m, j);
-        x.x -= acc[i][4 * h]; x.y -= acc[i][4 * h + 1];
-        x.z -= acc[i][4 * h + 2]; x.w -= acc[i][4 * h + 3];
-        Pb::store4(a, b, m, j, x);
+    for (int i = i0; i < i0 + 4; ++i) {
+      const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = n0 + (h ? 64 : 0) + tx * 4;
+        if (m < M && j < N) xs[i - i0][h] = Pb::c_load4(a, b, m, j);
+      }
+    }
+#pragma unroll
+    for (int i = i0; i < i0 + 4; ++i) {
+      const int m = m0 + (i < 4 ? ty * 4 + i : 64 + ty * 4 + i - 4);
+      if (m >= M) continue;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int j = n0 + (h ? 64 : 0) + tx * 4;
+        if (j < N) {
+          float4 x = xs[i - i0][h];
+          x.x -= acc[i][4 * h]; x.y -= acc[i][4 * h + 1];
+          x.z -= acc[i][4 * h + 2]; x.w -= acc[i][4 * h + 3];
+          Pb::store4(a, b, m, j, x);
+        }
       }
     }
   }

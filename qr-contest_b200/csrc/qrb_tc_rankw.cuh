@@ -130,16 +130,30 @@ __global__ void __launch_bounds__(NTHREADS, 3) tc_rankw_kernel(typename Pb::Args
   if (!ok) {
     if (tid == 0) atomicOr(Pb::info(a, b), INFO_DEVICE_TIMEOUT);
   } else {
-    // coalesced C read-modify-write: warp-wide 512-byte row segments
-#pragma unroll 4
-    for (int idx = tid; idx < 128 * 32; idx += NTHREADS) {
-      const int row = idx >> 5, c4 = (idx & 31) * 4;
-      const int m = m0 + row, j = n0 + c4;
-      if (m < M && j < N) {
-        float4 x = Pb::c_load4(a, b, m, j);
-        const float4 p = *reinterpret_cast<const float4*>(stage + row * RWT_STAGE_LD + c4);
-        x.x -= p.x; x.y -= p.y; x.z -= p.z; x.w -= p.w;
-        Pb::store4(a, b, m, j, x);
+    // coalesced C read-modify-write: warp-wide 512-byte row segments.  The loads of a group
+    // are all issued before its stores: C may be updated in place, so a load placed after a
+    // store could not be moved above it and every element would wait out its own round trip.
+    constexpr int IT = 128 * 32 / NTHREADS, G = 8;
+#pragma unroll
+    for (int g = 0; g < IT; g += G) {
+      float4 xs[G];
+#pragma unroll
+      for (int u = 0; u < G; ++u) {
+        const int idx = tid + (g + u) * NTHREADS;
+        const int m = m0 + (idx >> 5), j = n0 + (idx & 31) * 4;
+        if (m < M && j < N) xs[u] = Pb::c_load4(a, b, m, j);
+      }
+#pragma unroll
+      for (int u = 0; u < G; ++u) {
+        const int idx = tid + (g + u) * NTHREADS;
+        const int row = idx >> 5, c4 = (idx & 31) * 4;
+        const int m = m0 + row, j = n0 + c4;
+        if (m < M && j < N) {
+          float4 x = xs[u];
+          const float4 p = *reinterpret_cast<const float4*>(stage + row * RWT_STAGE_LD + c4);
+          x.x -= p.x; x.y -= p.y; x.z -= p.z; x.w -= p.w;
+          Pb::store4(a, b, m, j, x);
+        }
       }
     }
   }
