@@ -146,8 +146,8 @@ long long qrb200_launch_count(void);
  *   n % 4 == 0 and n > block.  qrb200_workspace_bytes reflects the value set when it is called. */
 #define QRB200_OPT_CHART_BLOCK 5
 /*   QRB200_OPT_PANEL_LOOP: column loop of the register-resident panels (panels of at most 512
- *   rows): 0 = automatic (default; panels of 129-256 rows then run two rows per thread of
- *   128 threads), 1 = fully unrolled, 2 = rotating registers (one column step of code, smaller
+ *   rows): 0 = automatic (default; LU and chart panels of at most 128 rows then run two rows
+ *   per thread of 64 threads, all panels of 129-256 rows two rows per thread of 128), 1 = fully unrolled, 2 = rotating registers (one column step of code, smaller
  *   than the instruction cache).  Modes 1 and 2 give bit-identical results. */
 #define QRB200_OPT_PANEL_LOOP 6
 int qrb200_set_option(int32_t key, int64_t value);

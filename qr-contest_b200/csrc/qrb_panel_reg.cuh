@@ -97,7 +97,7 @@ __device__ __forceinline__ void publish_multipliers(const float (&xr)[PR_W], flo
 // NT threads per CTA (256; 128 for panels of at most 128 rows, which then fit twice as many
 // CTAs per SM).
 template <int MODE, typename TIn, typename TOut, int RPT, int NT = 256, bool ROT = true>
-__global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : (NT == 128 ? 4 : 2)))
+__global__ void __launch_bounds__(NT, (RPT == 1 ? (NT == 128 ? 6 : 3) : (NT == 64 ? 8 : NT == 128 ? 4 : 2)))
     panel_reg_kernel(PanelArgs a) {
   constexpr int NWARP = NT / 32;
   const int n = a.n, k0 = a.k0, w = a.w, m = n - k0;
