@@ -150,6 +150,9 @@ long long qrb200_launch_count(void);
  *   per thread of 64 threads, all panels of 129-256 rows two rows per thread of 128), 1 = fully unrolled, 2 = rotating registers (one column step of code, smaller
  *   than the instruction cache).  Modes 1 and 2 give bit-identical results. */
 #define QRB200_OPT_PANEL_LOOP 6
+/*   QRB200_OPT_CLOSURE_DUAL_N: largest n (0..512, default 256) whose closure GEMM runs two CTAs
+ *   per SM; larger n use the one-CTA tile shape.  Results are identical either way. */
+#define QRB200_OPT_CLOSURE_DUAL_N 7
 int qrb200_set_option(int32_t key, int64_t value);
 
 /* Text of the last CUDA runtime error that made an entry point of this thread return

@@ -370,6 +370,8 @@ static cudaError_t ensure_attrs() {
 
 // Panels of at most 512 rows run register-resident (qrb_panel_reg.cuh); taller panels keep
 // the shared-memory panel kernel.
+// QRB200_OPT_CLOSURE_DUAL_N: largest n whose closure runs the two-CTAs-per-SM tile shape
+static std::atomic<int> g_closure_dual_n{256};
 // QRB200_OPT_PANEL_LOOP: 0 automatic, 1 unrolled column loop everywhere, 2 rotating loop
 static std::atomic<int> g_panel_loop{0};
 template <int MODE, typename TIn, typename TOut>
@@ -525,15 +527,18 @@ static void launch_small(const T* A, T* H, T* tau, int* info, int64_t cb, int n,
 
 // Explicit Q (optional output): householder_product(H, tau) = (I - Y T Y^T) = Q_frame * S,
 // because the chart factors I - Q_frame S = Y (T Y^T) (reflection_no_reflectors.py:86-176).
-// 16-bit input widened to float32 (n % 4 == 0: four elements per thread and step), the B
-// operand of the TMA-fed closure tile.
+// 16-bit input widened to float32 (n % 4 == 0, so the batch holds a multiple of 16 elements:
+// eight elements per thread and step, one 16-byte load and two 16-byte stores), the B operand
+// of the TMA-fed closure tile.
 template <typename T>
-__global__ void widen_kernel(const T* __restrict__ A, float* __restrict__ X, int64_t count4) {
-  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < count4;
+__global__ void widen_kernel(const T* __restrict__ A, float* __restrict__ X, int64_t count8) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < count8;
        q += (int64_t)gridDim.x * blockDim.x) {
-    const uint2 t = __ldg(reinterpret_cast<const uint2*>(A) + q);
+    const uint4 t = __ldg(reinterpret_cast<const uint4*>(A) + q);
     const T* h = reinterpret_cast<const T*>(&t);
-    reinterpret_cast<float4*>(X)[q] = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+    float4* o = reinterpret_cast<float4*>(X) + 2 * q;
+    o[0] = make_float4(to_f32(h[0]), to_f32(h[1]), to_f32(h[2]), to_f32(h[3]));
+    o[1] = make_float4(to_f32(h[4]), to_f32(h[5]), to_f32(h[6]), to_f32(h[7]));
   }
 }
 
@@ -689,19 +694,20 @@ static cudaError_t run_chunk(const T* A, T* H, T* tau, int* info, int64_t cb, in
   // bf16 matrices: closure 7.3 ms on the register-fed tile)
   tcx::Maps cm;
   constexpr bool f32 = std::is_same<T, float>::value;
-  const bool cx = tcp && (f32 || (reinterpret_cast<uintptr_t>(A) & 7) == 0) &&
+  const bool cx = tcp && (f32 || (reinterpret_cast<uintptr_t>(A) & 15) == 0) &&
                   tcx_maps(cm, ws.L, false, f32 ? static_cast<const void*>(A) : ws.T1, false, n, cb);
   if (cx && !f32) {
-    const int64_t c4 = cb * (int64_t)n * n / 4;
-    const unsigned gw = (unsigned)((c4 + 255) / 256 < 148 * 16 ? (c4 + 255) / 256 : 148 * 16);
-    QRB_LAUNCH(prof, F_CLOSURE, (widen_kernel<T><<<gw, 256, 0, st>>>(A, ws.T1, c4)));
+    const int64_t c8 = cb * (int64_t)n * n / 8;
+    const unsigned gw = (unsigned)((c8 + 255) / 256 < 148 * 32 ? (c8 + 255) / 256 : 148 * 32);
+    QRB_LAUNCH(prof, F_CLOSURE, (widen_kernel<T><<<gw, 256, 0, st>>>(A, ws.T1, c8)));
   }
   QRB_LAUNCH(prof, F_CLOSURE,
-             // the closure keeps the one-CTA shape at every K: its epilogue waits on global
-             // loads of A, and two CTAs per SM measured slower (2.51 -> 2.59 ms, n = 512)
+             // n <= 256 (QRB200_OPT_CLOSURE_DUAL_N) runs two CTAs per SM, larger n the one-CTA
+             // shape.  Closure ms, two vs one CTA per SM: n = 512 (1536) 2.63 vs 2.55; n = 256
+             // (8192) 2.69 vs 2.77, bf16 4.00 vs 4.32; n = 128 (16384) 1.19 vs 1.32.
              if (cx) launch_tcx<tcx::ClosureXT<T>>(tc_grid(n, n, cb), cm,
                                                tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info},
-                                               tcx::kDualMaxK + 1, st);
+                                               g_closure_dual_n.load() >= n ? n : tcx::kDualMaxK + 1, st);
              else if (tcp) tc::tc_gemm_kernel<tc::ClosureTC<T>, kTcBN>
                  <<<tc_grid(n, n, cb), tc::NTHREADS, kTcSmem, st>>>(
                      tc::ClosureTCArgs{n, ws.L, A, ws.s, H, info});
@@ -927,6 +933,11 @@ int qrb200_set_option(int32_t key, int64_t value) {
   if (key == QRB200_OPT_CHOL_BLOCK) {
     if (value != 0 && value != 64 && value != 128 && value != 256) return QRB200_ERR_INVALID_ARG;
     qrb::g_chol_block.store((int)value);
+    return QRB200_OK;
+  }
+  if (key == QRB200_OPT_CLOSURE_DUAL_N) {
+    if (value < 0 || value > qrb::tcx::kDualMaxK) return QRB200_ERR_INVALID_ARG;
+    qrb::g_closure_dual_n.store((int)value);
     return QRB200_OK;
   }
   if (key == QRB200_OPT_PANEL_LOOP) {

@@ -40,6 +40,7 @@ OPT_CHOL_BLOCK = 3
 OPT_LANES = 4
 OPT_CHART_BLOCK = 5
 OPT_PANEL_LOOP = 6
+OPT_CLOSURE_DUAL_N = 7
 GEMM_AUTO, GEMM_SIMT, GEMM_TC = 0, 1, 2
 
 # every symbol include/qrb200.h declares, with its ctypes signature
@@ -187,5 +188,12 @@ def set_chart_block(block: int) -> None:
 def set_panel_loop(mode: int) -> None:
     """Column loop of the register-resident panels: 0 automatic, 1 unrolled, 2 rotating."""
     rc = lib().qrb200_set_option(OPT_PANEL_LOOP, int(mode))
+    if rc != 0:
+        raise QRB200Error(rc, "qrb200_set_option")
+
+
+def set_closure_dual_n(n_max: int) -> None:
+    """Largest n whose closure GEMM runs two CTAs per SM (0 = none)."""
+    rc = lib().qrb200_set_option(OPT_CLOSURE_DUAL_N, int(n_max))
     if rc != 0:
         raise QRB200Error(rc, "qrb200_set_option")
