@@ -151,7 +151,8 @@ long long qrb200_launch_count(void);
  *   than the instruction cache).  Modes 1 and 2 give bit-identical results. */
 #define QRB200_OPT_PANEL_LOOP 6
 /*   QRB200_OPT_CLOSURE_DUAL_N: largest n (0..512, default 256) whose closure GEMM runs two CTAs
- *   per SM; larger n use the one-CTA tile shape.  Results are identical either way. */
+ *   per SM; larger n use the one-CTA tile shape (which adds its float32 partial sums every
+ *   256 k, so the two shapes agree to float32 rounding, not bit for bit). */
 #define QRB200_OPT_CLOSURE_DUAL_N 7
 int qrb200_set_option(int32_t key, int64_t value);
 

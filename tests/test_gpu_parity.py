@@ -281,6 +281,28 @@ def test_lanes_bit_identical(lanes):
     assert torch.equal(tau, t0) and torch.equal(info, i0)
 
 
+@pytest.mark.parametrize("n", [128, 256])
+def test_closure_tile_shapes(n):
+    """The closure GEMM in its two-CTAs-per-SM shape (default for n <= 256) and in the one-CTA
+    shape give the same upper triangle to float32 rounding; the chart part of H and tau do not
+    depend on it at all."""
+    from qrb200 import _lib, generators as G
+    A = G.gaussian((24, n, n), seed=59, device="cuda")
+    outs = []
+    try:
+        for d in (256, 0):
+            _lib.set_closure_dual_n(d)
+            outs.append(qrb().geqrf(A))
+    finally:
+        _lib.set_closure_dual_n(256)
+    (H1, t1, i1), (H2, t2, i2) = outs
+    up = torch.triu(torch.ones(n, n, dtype=torch.bool, device="cuda"))
+    assert torch.equal(t1, t2) and torch.equal(i1, i2)
+    assert torch.equal(H1[:, ~up], H2[:, ~up])
+    d = (H1 - H2).abs()[:, up]
+    assert float((d / (1 + H2.abs()[:, up])).max()) <= 2e-5
+
+
 @pytest.mark.parametrize("n", [66, 100, 130, 257, 384, 512])
 def test_panel_loops_bit_identical(n):
     """The register panels' two column loops (fully unrolled; rotating registers) perform the
