@@ -494,7 +494,7 @@ def measure_c5(dev, rank, world):
 
     def step():
         out["r"] = qrb200.geqrf(A, workspace=ws)
-    ms = dev_time(step, dev, reps=2, warm=1, world=world)
+    ms = dev_time(step, dev, reps=4, warm=1, world=world)
     H, tau, info = out["r"]
     del ws
     # per-family CUDA-event timings of the library on the first 8192 matrices of the shard
